@@ -1,0 +1,236 @@
+/*
+ * kvs.h -- C ABI of the B200 KV block store (kvcache_manager hot path).
+ *
+ * This is the drop-in boundary that replaces the reference's TTNN backend bridge
+ * (src/backend_bridge.hpp:16-28, which pins the opaque ClientOperations ABI, version 4, of
+ * third_party/tt-metal/patches/0003-kvcache-protocol-device-runtime.patch lines 3408-3531).
+ * Every entry point takes plain pointers and sizes; device buffers are CUDA device pointers
+ * (or any UVA pointer the CUDA device can address) and streams are cudaStream_t passed as
+ * void*. No C++ or torch types cross this boundary.
+ *
+ * Conventions
+ *   - Every function returns KVS_OK (0) or a negative KVS_E_* code; kvs_last_error() returns a
+ *     thread-local message for the last failure on the calling thread. A get miss is not an
+ *     error: *found is set to 0.
+ *   - Calls on one client are serialised by the client; distinct clients may call
+ *     concurrently. A shard (kvs_server) serialises the directory updates of all its clients.
+ *   - Keys are 1..max_key_bytes (<= 128) bytes. The batched block calls take 64-bit keys
+ *     (chained prefix-block hashes); a 64-bit key is stored as its 8 little-endian bytes, so
+ *     kvs_put(key=&u64, key_len=8) and kvs_put_blocks(keys={u64}) name the same entry.
+ *   - Ordering follows the reference (design.md sections 5-6, patch 0003 lines 7527-7683): a put
+ *     returns once its bytes have landed in the device slab (on `stream`); host write-through
+ *     finishes asynchronously; get, exists, delete, move and flush first wait for every issued
+ *     put to be host-committed (the reference's COMMIT_BARRIER).
+ */
+#ifndef KVS_H
+#define KVS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KVS_ABI_VERSION 1
+
+/* status codes */
+#define KVS_OK 0
+#define KVS_E_INVAL (-1)       /* invalid argument (reference: TT_FATAL on validation) */
+#define KVS_E_CUDA (-2)        /* a CUDA call failed */
+#define KVS_E_NOSPACE (-3)     /* no device-cache or catalog space even after forced commits */
+#define KVS_E_TIMEOUT (-4)     /* a bounded wait expired */
+#define KVS_E_TOO_SMALL (-5)   /* get: output capacity smaller than the stored value */
+#define KVS_E_QUARANTINED (-6) /* an earlier indeterminate failure quarantined this handle */
+#define KVS_E_CLOSED (-7)      /* the handle was closed */
+#define KVS_E_FORMAT (-8)      /* stored value does not match the requested block layout */
+
+/* location codes reported by kvs_location (reference layout.hpp kLocation*) */
+#define KVS_LOC_DEVICE 0
+#define KVS_LOC_HOST 1
+#define KVS_LOC_PENDING 2
+#define KVS_LOC_ABSENT (-1)
+
+typedef struct kvs_server kvs_server; /* one store shard, owning one GPU's slab */
+typedef struct kvs_client kvs_client; /* a client bound to one GPU and a set of shards */
+
+/* Server construction knobs. Replaces the reference's env-parsed ServerRuntimeCore config
+ * (src/native/ttnn/server_runtime/server.cpp:199-350; patch 0003 lines 5156-5380). */
+typedef struct {
+  int32_t device;           /* CUDA device ordinal that holds the slab and index */
+  uint32_t max_keys;        /* catalog entries (KVM_SERVER_DRAM_MAX_KEYS) */
+  uint32_t unit_bytes;      /* value-heap unit; 4288 = the reference's kMaxChunkValueBytes */
+  uint32_t max_key_bytes;   /* <= 128 (KVM_SERVER_MAX_KEY_BYTES) */
+  uint64_t heap_bytes;      /* device value slab (KVM_SERVER_DRAM_VALUE_HEAP_BYTES) */
+  uint64_t host_pool_bytes; /* pinned host pool (KVM_SERVER_HOST_POOL_BYTES) */
+  uint64_t max_value_bytes; /* per-value cap (KVM_COMMON_MAX_VALUE_BYTES) */
+  uint32_t shard_id;        /* this shard's index in a hash-sharded group */
+  uint32_t flags;           /* KVS_SERVER_* bits */
+} kvs_server_config;
+
+#define KVS_SERVER_PROFILE 1u /* collect move timing (KVM_SERVER_PROFILE) */
+
+/* Paged KV layout the block calls gather from / scatter into. A value stored for one key is
+ * the one-block chunk blob of the reference's raw-byte codec (patch 0005 lines 12258-12310):
+ *   header words [0x524B564E, n_layers, bytes_of_layer(0) .. bytes_of_layer(n_layers-1)]
+ *   zero padded to 32 bytes, then every member's block back to back in member order.
+ * Members are grouped per layer (members_per_layer of them: K, V, and optionally per-block
+ * scales), member m of layer l is member_ptrs[l * members_per_layer + m]. */
+typedef struct {
+  uint32_t n_members;                /* total members = n_layers * members_per_layer */
+  uint32_t members_per_layer;        /* 2 for (K, V) */
+  const uint64_t *member_ptrs;       /* [n_members] device pointers (host array) */
+  const uint64_t *member_block_bytes;/* [n_members] bytes of one block of each member */
+  uint64_t n_pool_blocks;            /* blocks per member tensor (bounds check) */
+} kvs_block_layout;
+
+typedef struct {
+  uint64_t count;
+  uint64_t prepare_ns;
+  uint64_t program_ns;
+  uint64_t enqueue_ns;
+  uint64_t landed_wait_ns;
+  uint64_t commit_wait_ns;
+  uint64_t total_ns;
+} kvs_put_profile; /* include/kvcache_manager/profiles.hpp:43-51 PutProfile */
+
+typedef struct {
+  uint64_t to_host_count, to_host_worker_ns, to_host_complete_ns, to_host_read_calls,
+      to_host_read_bytes, to_host_read_passes, to_host_read_retries, to_host_read_io_ns,
+      to_host_scatter_ns, to_host_device_pushes, to_device_count, to_device_worker_ns,
+      to_device_complete_ns;
+} kvs_move_profile; /* profiles.hpp:10-24 MoveProfile */
+
+typedef struct {
+  uint64_t allocation_calls, allocation_successes, allocation_failures, victim_scans,
+      victims_evicted, lease_calls, lease_successes, lease_failures, lease_victim_scans,
+      lease_victims_evicted, scan_cycles, lease_scan_cycles, allocation_cycles;
+  uint32_t clock_mhz;
+} kvs_allocator_profile; /* profiles.hpp:26-41 AllocatorProfile */
+
+typedef struct {
+  uint64_t live_device_bytes, pending_device_bytes, live_keys, device_resident_keys;
+  uint64_t allocation_calls, allocation_successes, allocation_failures, victims_evicted;
+  uint64_t catalog_replacements, writes_through, stale_commits, host_serves, admissions;
+  uint64_t pool_values, heap_values;
+  uint32_t epoch, issued, committed;
+  uint64_t kernel_launches; /* kernels this shard's clients launched */
+} kvs_stats;
+
+/* ---- version / errors ---- */
+int kvs_abi_version(void);        /* replaces client_operations_abi_version(), patch 0003:3439 */
+const char *kvs_last_error(void); /* thread-local message of the last failure */
+
+/* ---- server (one shard) ----  include/kvcache_manager/server.hpp:21-55 */
+int kvs_server_config_default(kvs_server_config *cfg); /* defaults + KVM_* environment knobs */
+int kvs_server_create(const kvs_server_config *cfg, kvs_server **out);
+int kvs_server_destroy(kvs_server *s); /* drains write-through, then frees (Server::close) */
+int kvs_server_is_ready(kvs_server *s, int *ready);
+int kvs_server_moves_completed(kvs_server *s, uint64_t *out);
+int kvs_server_move_profile(kvs_server *s, kvs_move_profile *out);
+int kvs_server_allocator_profile(kvs_server *s, kvs_allocator_profile *out);
+int kvs_server_stats(kvs_server *s, kvs_stats *out);
+int kvs_server_device(kvs_server *s, int *device);
+/* commit_barrier progress: issued and committed PUT counters (Server::test_put_drain_progress,
+ * server.hpp:52) */
+int kvs_server_put_drain_progress(kvs_server *s, uint32_t *issued, uint32_t *committed);
+/* introspection for parity tests: location of a key (KVS_LOC_*), and its slab offset */
+int kvs_server_location(kvs_server *s, const void *key, uint32_t key_len, int *location,
+                        uint64_t *value_off);
+/* copies the host directory's hash buckets ({hash, slot} pairs) and the device replica's */
+int kvs_server_index_snapshot(kvs_server *s, uint32_t *host_pairs, uint32_t *device_pairs,
+                              uint32_t cap_pairs, uint32_t *n_buckets);
+/* residency LRU from MRU to LRU as directory slots */
+int kvs_server_lru_order(kvs_server *s, uint32_t *slots, uint32_t cap, uint32_t *n);
+
+/* ---- client ----  include/kvcache_manager/client.hpp:26-66 */
+/* A client on `device` addressing `n_shards` shards; key k goes to shard fnv1a32(k) % n_shards
+ * (the reference's worker groups, server.cpp:80-86, become hash shards across GPUs). */
+int kvs_client_create(kvs_server *const *shards, uint32_t n_shards, int32_t device,
+                      kvs_client **out);
+int kvs_client_destroy(kvs_client *c); /* drains this client's puts, then frees (Client::close) */
+int kvs_client_is_established(kvs_client *c, int *established);
+int kvs_client_shard_of(kvs_client *c, const void *key, uint32_t key_len, uint32_t *shard);
+/* PING: echo payload (<= 1024 bytes) through the device (Client::ping) */
+int kvs_ping(kvs_client *c, const void *payload, uint32_t len, void *out, void *stream);
+
+/* Client::put (patch 0003 lines 2533-2651): store value_len bytes at `value` (device memory)
+ * under key. Returns after the bytes landed in the slab; sync_commit also waits for host
+ * write-through. */
+int kvs_put(kvs_client *c, const void *key, uint32_t key_len, const void *value,
+            uint64_t value_len, int sync_commit, void *stream);
+/* Client::put_batch: n independent puts in input order */
+int kvs_put_batch(kvs_client *c, uint32_t n, const void *const *keys, const uint32_t *key_lens,
+                  const void *const *values, const uint64_t *value_lens, int sync_commit,
+                  void *stream);
+/* Client::get (patch 0003 lines 2786-2891): on a hit, copy the value into out (capacity bytes)
+ * and set *found=1, *value_len; a miss leaves out unchanged. */
+int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_t capacity,
+            int *found, uint64_t *value_len, void *stream);
+/* Client::get_parallel (patch 0003 lines 2893-3125): clients[i] reads keys[i] into
+ * out + i * stride; found[i] per key. */
+int kvs_get_parallel(kvs_client *const *clients, uint32_t n, const void *const *keys,
+                     const uint32_t *key_lens, void *out, uint64_t stride, uint64_t capacity,
+                     uint8_t *found, void *stream);
+int kvs_exists(kvs_client *c, const void *key, uint32_t key_len, int *found);
+int kvs_delete(kvs_client *c, const void *key, uint32_t key_len, int *removed);
+int kvs_move_to_host(kvs_client *c, const void *key, uint32_t key_len);
+int kvs_move_to_device(kvs_client *c, const void *key, uint32_t key_len);
+int kvs_flush(kvs_client *c);
+int kvs_client_put_profile(kvs_client *c, kvs_put_profile *out);
+
+/* ---- batched paged-block path (the B200 main path) ----
+ * put: for each i, gather block block_ids[i] of every member into one blob value stored under
+ *      keys[i] (one kernel for the whole batch). Replaces the connector's per-chunk
+ *      gather_tp_shards_to_chip + Client.put sequence (patch 0005 lines 9653-9708).
+ * get: look every key up in the shard's device hash index (warp-cooperative probe) and
+ *      scatter each hit's members into block block_ids[i]; found[i] per key (host array).
+ *      Misses leave their blocks untouched. Replaces Client.get + scatter_chunk_from_chip.
+ * keys / block_ids / found are host arrays. */
+int kvs_put_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n,
+                   const uint64_t *keys, const int64_t *block_ids, int sync_commit,
+                   void *stream);
+int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n,
+                   const uint64_t *keys, const int64_t *block_ids, uint8_t *found,
+                   void *stream);
+/* EXISTS over a batch of 64-bit keys through the device index; no recency update. */
+int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found);
+
+/* ---- chunk gather / scatter ops ----
+ * gather_tp_shards_to_chip / pack_local_shards (patch 0003 gather.hpp lines 9372-9417) and
+ * their inverses scatter_chunk_from_chip / unpack_local_shards (9418-9453).
+ * member_ptrs[r * n_members + m] is rank r's shard of member m (device or peer pointers);
+ * for member m, chunk block cb and rank r, member_block_bytes[m] bytes at
+ * block_ids[cb] * member_block_bytes[m] move to/from
+ * blob + region_bases[m] + cb * member_block_bytes[m] * n_ranks + r * member_block_bytes[m].
+ * gather writes header_words at the blob start. member_extent[m] bounds every member buffer,
+ * blob_bytes bounds the blob; violations return KVS_E_INVAL before any access. Asynchronous on
+ * `stream` (on the device of `blob`). */
+int kvs_gather_chunk(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_members,
+                     const uint64_t *member_block_bytes, const uint64_t *member_extent,
+                     const uint32_t *block_ids, uint32_t n_blocks, const uint64_t *region_bases,
+                     const uint32_t *header_words, uint32_t n_header_words, void *blob,
+                     uint64_t blob_bytes, void *stream);
+int kvs_scatter_chunk(const void *blob, uint64_t blob_bytes, const uint64_t *member_ptrs,
+                      uint32_t n_ranks, uint32_t n_members, const uint64_t *member_block_bytes,
+                      const uint64_t *member_extent, const uint32_t *block_ids,
+                      uint32_t n_blocks, const uint64_t *region_bases, void *stream);
+
+/* kernels launched by this library since load (a launch counter for the benchmark) */
+uint64_t kvs_kernel_launch_count(void);
+
+/* Per-client kernel timing: with timing on, CUDA events bracket every gather (put) and scatter
+ * (get) copy-engine launch on the client stream. kvs_client_timing waits for them, returns the
+ * totals since the last call (and resets). bytes = payload bytes the kernels moved. */
+typedef struct {
+  uint64_t launches;
+  uint64_t bytes;
+  double total_ms;
+} kvs_kernel_timing;
+int kvs_client_set_timing(kvs_client *c, int enable);
+int kvs_client_timing(kvs_client *c, kvs_kernel_timing *gather, kvs_kernel_timing *scatter);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVS_H */

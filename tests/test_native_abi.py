@@ -1,0 +1,107 @@
+"""The C ABI library loads on CPU and exports exactly what include/kvs.h declares.
+
+No compute call runs here (there is no GPU): only symbol presence, the ABI version, the
+environment-knob parsing of kvs_server_config_default, and argument validation that fails before
+touching a device.
+"""
+
+import ctypes as C
+import os
+import re
+from pathlib import Path
+
+import pytest
+
+from kvcache_manager import _native
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "kvs.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(kvs_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _native.load()
+
+
+def test_every_declared_symbol_is_exported_and_bound(lib):
+    names = declared_functions()
+    assert len(names) >= 35
+    raw = C.CDLL(str(_native.LIB_PATH))
+    for n in names:
+        assert hasattr(raw, n), f"{n} declared in kvs.h but not exported"
+    assert set(names) == set(_native.SIGNATURES), set(names) ^ set(_native.SIGNATURES)
+
+
+def test_abi_version(lib):
+    assert lib.kvs_abi_version() == _native.KVS_ABI_VERSION == 1
+
+
+def test_config_defaults_restate_reference_defaults(lib, monkeypatch):
+    for k in ("KVM_SERVER_DRAM_MAX_KEYS", "KVM_SERVER_DRAM_VALUE_HEAP_BYTES", "KVM_SERVER_HOST_POOL_BYTES",
+              "KVM_COMMON_MAX_VALUE_BYTES", "KVM_SERVER_MAX_KEY_BYTES"):
+        monkeypatch.delenv(k, raising=False)
+    cfg = _native.ServerConfig()
+    assert lib.kvs_server_config_default(C.byref(cfg)) == 0
+    assert cfg.max_keys == 1024  # kMaxKeysDefault
+    assert cfg.heap_bytes == 1_434_541_824  # kValueHeapBytesDefault
+    assert cfg.unit_bytes == 4288  # kMaxChunkValueBytes
+    assert cfg.max_key_bytes == 128  # kMaxPutKeyBytes
+    assert cfg.max_value_bytes == 64 << 20  # kMaxMultiChunkValueBytesDefault
+
+
+@pytest.mark.parametrize("bad", ["", " 1", "1 ", "+1", "-1", "1x", "18446744073709551616"])
+def test_config_env_parsing_is_exact(lib, monkeypatch, bad):
+    monkeypatch.setenv("KVM_SERVER_DRAM_MAX_KEYS", bad)
+    cfg = _native.ServerConfig()
+    assert lib.kvs_server_config_default(C.byref(cfg)) == _native.E_INVAL
+    assert b"KVM_SERVER_DRAM_MAX_KEYS" in lib.kvs_last_error()
+
+
+def test_config_env_overrides(lib, monkeypatch):
+    monkeypatch.setenv("KVM_SERVER_DRAM_MAX_KEYS", "1048576")
+    monkeypatch.setenv("KVM_SERVER_MAX_KEY_BYTES", "64")
+    cfg = _native.ServerConfig()
+    assert lib.kvs_server_config_default(C.byref(cfg)) == 0
+    assert cfg.max_keys == 1 << 20 and cfg.max_key_bytes == 64
+    monkeypatch.setenv("KVM_SERVER_MAX_KEY_BYTES", "129")
+    assert lib.kvs_server_config_default(C.byref(cfg)) == _native.E_INVAL
+
+
+def test_null_and_invalid_arguments_fail_without_a_device(lib):
+    h = C.c_void_p()
+    assert lib.kvs_server_create(None, C.byref(h)) == _native.E_INVAL
+    assert lib.kvs_client_create(None, 0, 0, C.byref(h)) == _native.E_INVAL
+    assert lib.kvs_server_destroy(None) == 0
+    assert lib.kvs_client_destroy(None) == 0
+    found = C.c_int()
+    assert lib.kvs_exists(None, b"k", 1, C.byref(found)) == _native.E_INVAL
+    # chunk op validation runs before any device access
+    ptrs = (C.c_uint64 * 1)(1)
+    sbb = (C.c_uint64 * 1)(30)  # not 4-byte aligned
+    ext = (C.c_uint64 * 1)(1 << 20)
+    ids = (C.c_uint32 * 1)(0)
+    rb = (C.c_uint64 * 1)(32)
+    assert lib.kvs_gather_chunk(ptrs, 1, 1, sbb, ext, ids, 1, rb, None, 0, C.c_void_p(1), 1 << 20, None) == _native.E_INVAL
+    assert b"4-byte aligned" in lib.kvs_last_error()
+    sbb[0] = 32
+    hw = (C.c_uint32 * 4)(1, 2, 3, 4)  # 16-byte header
+    assert lib.kvs_gather_chunk(ptrs, 1, 1, sbb, ext, ids, 1, rb, hw, 4, C.c_void_p(1), 1 << 20, None) == _native.E_INVAL
+    assert b"header must be 32-byte aligned" in lib.kvs_last_error()
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    with pytest.raises(ImportError, match="requires its native extension"):
+        _native.load(tmp_path / "libkvs_b200.so")
+
+
+def test_oracle_is_not_importable_from_the_product():
+    pkg = Path(__file__).resolve().parents[1] / "tt-infinity_b200"
+    for p in pkg.rglob("*"):
+        if p.suffix in (".py", ".cu", ".cuh", ".cpp", ".hpp", ".h"):
+            assert "oracle" not in p.read_text().replace("oracles", ""), p
+    assert os.path.exists(_native.LIB_PATH)

@@ -1,0 +1,256 @@
+// kvs_kernels.cu -- sm_100a kernels of the B200 KV block store. See kvs_kernels.cuh.
+#include "kvs_kernels.cuh"
+
+#include <atomic>
+
+namespace kvs {
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+constexpr int kCopyThreads = 512;
+constexpr int kCopyUnroll = 4;  // 16-byte vectors in flight per thread per step
+
+__device__ __forceinline__ int4 ld_stream(const int4 *p) {
+  int4 v;
+  asm volatile("ld.global.cs.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_stream(int4 *p, const int4 &v) {
+  asm volatile("st.global.cs.v4.s32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// CTA-wide copy of `len` bytes. 16-byte path when both ends and the length are 16-byte aligned
+// (every KV block segment of the paged layouts), else a 4-byte or byte path.
+__device__ __forceinline__ void cta_copy(uint8_t *dst, const uint8_t *src, uint64_t len) {
+  const uint64_t align = reinterpret_cast<uint64_t>(dst) | reinterpret_cast<uint64_t>(src) | len;
+  const uint32_t tid = threadIdx.x;
+  if ((align & 15u) == 0) {
+    const int4 *s = reinterpret_cast<const int4 *>(src);
+    int4 *d = reinterpret_cast<int4 *>(dst);
+    const uint64_t n = len >> 4;
+    const uint64_t step = (uint64_t)blockDim.x * kCopyUnroll;
+    for (uint64_t base = tid; base < n; base += step) {
+      int4 v[kCopyUnroll];
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const uint64_t i = base + (uint64_t)u * blockDim.x;
+        if (i < n) v[u] = ld_stream(s + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kCopyUnroll; ++u) {
+        const uint64_t i = base + (uint64_t)u * blockDim.x;
+        if (i < n) st_stream(d + i, v[u]);
+      }
+    }
+  } else if ((align & 3u) == 0) {
+    const uint32_t *s = reinterpret_cast<const uint32_t *>(src);
+    uint32_t *d = reinterpret_cast<uint32_t *>(dst);
+    for (uint64_t i = tid; i < (len >> 2); i += blockDim.x) d[i] = s[i];
+  } else {
+    for (uint64_t i = tid; i < len; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
+__global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const ChunkCopyParams p) {
+  // Header words: one thread per (blob, word) -- gather only.
+  if (p.to_blob && p.n_header_words) {
+    const uint64_t nh = (uint64_t)p.n_blobs * p.n_header_words;
+    for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < nh;
+         g += (uint64_t)gridDim.x * blockDim.x) {
+      const uint32_t b = (uint32_t)(g / p.n_header_words), w = (uint32_t)(g % p.n_header_words);
+      const uint64_t base = p.blob_ptrs[b];
+      if (base) reinterpret_cast<uint32_t *>(base)[w] = p.header_words[w];
+    }
+  }
+  const uint64_t tpc = p.tiles_per_combo;
+  for (uint64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+    const uint64_t combo = t / tpc;
+    const uint64_t rem = t - combo * tpc;
+    // member m: tile_prefix[m] <= rem < tile_prefix[m + 1] (binary search, uniform per CTA)
+    uint32_t lo = 0, hi = p.n_members;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (p.tile_prefix[mid] <= rem) lo = mid; else hi = mid;
+    }
+    const uint32_t m = lo;
+    const uint64_t tile_in_seg = rem - p.tile_prefix[m];
+    const uint32_t r = (uint32_t)(combo % p.n_ranks);
+    const uint64_t bc = combo / p.n_ranks;
+    const uint32_t cb = (uint32_t)(bc % p.blocks_per_blob);
+    const uint32_t blob = (uint32_t)(bc / p.blocks_per_blob);
+    const uint64_t blob_base = p.blob_ptrs[blob];
+    if (blob_base == 0) continue;
+    const uint64_t sbb = p.member_bytes[m];
+    const uint64_t seg_off = tile_in_seg * p.tile_bytes;
+    const uint64_t len = (sbb - seg_off) < p.tile_bytes ? (sbb - seg_off) : p.tile_bytes;
+    const int64_t block = p.block_ids[(uint64_t)blob * p.blocks_per_blob + cb];
+    uint8_t *member = reinterpret_cast<uint8_t *>(p.member_ptrs[(uint64_t)r * p.n_members + m]) +
+                      (uint64_t)block * sbb + seg_off;
+    uint8_t *blob_ptr = reinterpret_cast<uint8_t *>(blob_base) + p.region_bases[m] +
+                        (uint64_t)cb * sbb * p.n_ranks + (uint64_t)r * sbb + seg_off;
+    if (p.to_blob)
+      cta_copy(blob_ptr, member, len);
+    else
+      cta_copy(member, blob_ptr, len);
+  }
+}
+
+// One warp per key. Lane i holds key word i; lane 0 computes the FNV-1a hash.
+__global__ void index_lookup_kernel(const LookupParams p) {
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+  if (warp >= p.n) return;
+  const uint8_t *key = p.keys + (uint64_t)warp * p.key_stride;
+  const uint32_t klen = p.key_lens ? p.key_lens[warp] : p.key_stride;
+  // key word of this lane, zero padded past klen (directory rows are zero padded too)
+  uint32_t kw = 0;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t i = lane * 4 + b;
+    if (i < klen) kw |= (uint32_t)key[i] << (8 * b);
+  }
+  uint32_t h = 0;
+  if (lane == 0) {
+    h = 2166136261u;
+    for (uint32_t i = 0; i < klen; ++i) {
+      h ^= key[i];
+      h *= 16777619u;
+    }
+  }
+  h = __shfl_sync(0xFFFFFFFFu, h, 0);
+  const uint32_t mask = p.bucket_mask;
+  uint32_t idx = h & mask;
+  uint32_t found_slot = kBucketEmpty;
+  const uint32_t windows = (mask >> 5) + 2;
+  for (uint32_t w = 0; w < windows && found_slot == kBucketEmpty; ++w) {
+    const uint64_t b = p.buckets[(idx + lane) & mask];
+    const uint32_t slot = (uint32_t)(b >> 32);
+    const uint32_t bh = (uint32_t)b;
+    const uint32_t empty = __ballot_sync(0xFFFFFFFFu, slot == kBucketEmpty);
+    uint32_t cand = __ballot_sync(0xFFFFFFFFu, slot < p.max_keys && bh == h);
+    const uint32_t first_empty = empty ? (uint32_t)(__ffs(empty) - 1) : 32u;
+    if (first_empty < 32) cand &= (1u << first_empty) - 1u;
+    while (cand) {
+      const uint32_t c = __ffs(cand) - 1;
+      const uint32_t cslot = __shfl_sync(0xFFFFFFFFu, slot, c);
+      const DevMeta m = p.meta[cslot];
+      const uint32_t row_word = p.key_rows[(uint64_t)cslot * kKeyRowWords + lane];
+      const bool eq = __all_sync(0xFFFFFFFFu, row_word == kw);
+      if (eq && m.valid && m.key_len == klen) {
+        found_slot = cslot;
+        break;
+      }
+      cand &= cand - 1;
+    }
+    if (found_slot != kBucketEmpty || first_empty < 32) break;
+    idx = (idx + 32) & mask;
+  }
+  if (lane == 0) {
+    LookupOut o{};
+    uint64_t blob = 0;
+    if (found_slot != kBucketEmpty) {
+      const DevMeta m = p.meta[found_slot];
+      o.slot = found_slot;
+      o.value_off = m.value_off;
+      o.value_len = m.total_len;
+      if (p.expected_len && m.total_len != p.expected_len)
+        o.status = kLenMismatch;
+      else if (m.location == 1)
+        o.status = kHitHost;
+      else {
+        o.status = kHitDevice;
+        blob = p.slab_base + m.value_off;
+      }
+    } else {
+      o.slot = kBucketEmpty;
+      o.status = kMiss;
+    }
+    p.out[warp] = o;
+    if (p.blob_ptrs) p.blob_ptrs[warp] = blob;
+  }
+}
+
+__global__ void apply_mutations_kernel(const MutationParams p) {
+  const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = tid; i < p.n_bucket_writes; i += stride)
+    p.buckets[p.bucket_writes[2 * i]] = p.bucket_writes[2 * i + 1];
+  for (uint64_t i = tid; i < p.n_meta_writes; i += stride) {
+    const uint64_t slot = p.meta_writes[3 * i];
+    uint64_t *dst = reinterpret_cast<uint64_t *>(p.meta + slot);
+    dst[0] = p.meta_writes[3 * i + 1];
+    dst[1] = p.meta_writes[3 * i + 2];
+  }
+  const uint64_t kw = (uint64_t)p.n_key_writes * kKeyRowWords;
+  for (uint64_t i = tid; i < kw; i += stride) {
+    const uint64_t row = i / kKeyRowWords, word = i % kKeyRowWords;
+    const uint32_t *rec = p.key_writes + row * (kKeyRowWords + 1);
+    p.key_rows[(uint64_t)rec[0] * kKeyRowWords + word] = rec[1 + word];
+  }
+}
+
+__global__ void echo_kernel(const uint8_t *in, uint8_t *out, uint32_t n) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    out[i] = in[i];
+}
+
+int sm_count() {
+  static int count = 0;
+  if (count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev);
+    if (count <= 0) count = 148;
+  }
+  return count;
+}
+
+}  // namespace
+
+cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas) {
+  if (p.total_tiles == 0 && (p.n_header_words == 0 || !p.to_blob)) return cudaSuccess;
+  uint64_t grid = grid_ctas > 0 ? (uint64_t)grid_ctas : (uint64_t)sm_count() * (2048 / kCopyThreads);
+  if (grid > p.total_tiles && p.total_tiles > 0) grid = p.total_tiles;
+  if (grid == 0) grid = 1;
+  chunk_copy_kernel<<<(unsigned)grid, kCopyThreads, 0, stream>>>(p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream) {
+  if (p.n == 0) return cudaSuccess;
+  const uint32_t threads = 256, warps_per_cta = threads / 32;
+  const uint32_t grid = (p.n + warps_per_cta - 1) / warps_per_cta;
+  index_lookup_kernel<<<grid, threads, 0, stream>>>(p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream) {
+  const uint64_t work = (uint64_t)p.n_bucket_writes + p.n_meta_writes +
+                        (uint64_t)p.n_key_writes * kKeyRowWords;
+  if (work == 0) return cudaSuccess;
+  uint64_t grid = (work + 255) / 256;
+  if (grid > 1024) grid = 1024;
+  apply_mutations_kernel<<<(unsigned)grid, 256, 0, stream>>>(p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_echo(const uint8_t *in, uint8_t *out, uint32_t n, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  echo_kernel<<<1, 256, 0, stream>>>(in, out, n);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+uint64_t kernel_launches() { return g_launches.load(std::memory_order_relaxed); }
+
+}  // namespace kvs

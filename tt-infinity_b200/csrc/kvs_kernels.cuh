@@ -1,0 +1,120 @@
+// kvs_kernels.cuh -- device-side data structures and kernel launchers of the B200 KV block store.
+//
+// Three kernel families move every byte and answer every device-side lookup:
+//   * chunk_copy: the paged-block gather (put) / scatter (get) engine. It moves whole member
+//     blocks between paged KV tensors and packed blobs (device slab values or caller blobs),
+//     16-byte vectorised and coalesced, tiles spread over a persistent grid of 148 x k CTAs.
+//     It restates the byte layout of gather_tp_shards_to_chip / scatter_chunk_from_chip
+//     (patch 0003 gather.hpp lines 9372-9453) for one GPU or for peer GPUs over NVLink.
+//   * index_lookup: a warp-cooperative probe of the shard's device replica of the FNV-1a
+//     open-addressed index (patch 0003 lines 9923-9963): 32 buckets per probe step, ballot
+//     for empty / hash-matching lanes, and a 32-lane key compare against the directory row.
+//   * apply_mutations: brings the device index replica up to date with the host directory
+//     (bucket words, entry metadata, key rows) in stream order before any lookup reads it.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace kvs {
+
+constexpr uint32_t kBucketEmpty = 0xFFFFFFFFu;      // reference kBucketDirSlotEmpty
+constexpr uint32_t kBucketTombstone = 0xFFFFFFFEu;  // reference kBucketDirSlotTombstone
+constexpr uint32_t kMaxKeyBytes = 128;              // reference kMaxPutKeyBytes
+constexpr uint32_t kKeyRowWords = kMaxKeyBytes / 4; // 32 words = one per lane
+
+// Device replica of one directory entry (16 bytes). location: 0 device, 1 host, 2 pending.
+struct alignas(16) DevMeta {
+  uint64_t value_off;
+  uint32_t total_len;
+  uint8_t valid;
+  uint8_t location;
+  uint8_t key_len;
+  uint8_t pad;
+};
+static_assert(sizeof(DevMeta) == 16, "DevMeta is one 16-byte word");
+
+// Lookup result per key (written by index_lookup).
+enum LookupStatus : uint32_t {
+  kMiss = 0,
+  kHitDevice = 1,   // device-resident (or pending, which is device-readable)
+  kHitHost = 2,     // host-only: the host tier serves it
+  kLenMismatch = 3, // hit, but the stored value length differs from the expected block value
+};
+
+struct LookupOut {
+  uint64_t value_off;
+  uint32_t value_len;
+  uint32_t status;
+  uint32_t slot;
+  uint32_t pad;
+};
+
+// Parameters of one chunk_copy launch. All arrays are device-accessible.
+struct ChunkCopyParams {
+  const uint64_t *member_ptrs;   // [n_ranks * n_members]
+  const uint64_t *member_bytes;  // [n_members] bytes of one block of the member
+  const uint64_t *region_bases;  // [n_members] member region offset inside a blob
+  const uint64_t *tile_prefix;   // [n_members + 1] tiles per member, prefix summed
+  const int64_t *block_ids;      // [n_blobs * blocks_per_blob]
+  const uint64_t *blob_ptrs;     // [n_blobs] blob base addresses; 0 skips the blob
+  const uint32_t *header_words;  // [n_header_words] (gather only)
+  uint32_t n_header_words;
+  uint32_t n_blobs;
+  uint32_t blocks_per_blob;
+  uint32_t n_ranks;
+  uint32_t n_members;
+  uint32_t tile_bytes;
+  uint64_t tiles_per_combo;  // tile_prefix[n_members]
+  uint64_t total_tiles;
+  int to_blob;               // 1: members -> blob (gather), 0: blob -> members (scatter)
+};
+
+struct LookupParams {
+  const uint8_t *keys;      // n keys, `key_stride` bytes apart
+  const uint32_t *key_lens; // nullptr: every key is key_stride bytes
+  uint32_t key_stride;
+  uint32_t n;
+  const uint64_t *buckets;  // (slot << 32) | hash
+  uint32_t bucket_mask;
+  const DevMeta *meta;
+  const uint32_t *key_rows; // [max_keys][kKeyRowWords]
+  uint32_t max_keys;
+  uint64_t slab_base;       // device address of the slab
+  uint64_t expected_len;    // 0: any length
+  LookupOut *out;
+  uint64_t *blob_ptrs;      // optional: slab_base + off for device hits, else 0
+};
+
+struct MutationParams {
+  const uint64_t *bucket_writes;  // pairs {bucket index, bucket word}
+  uint32_t n_bucket_writes;
+  const uint64_t *meta_writes;    // triples {slot, meta word 0, meta word 1}
+  uint32_t n_meta_writes;
+  const uint32_t *key_writes;     // rows of {slot, kKeyRowWords words}
+  uint32_t n_key_writes;
+  uint64_t *buckets;
+  DevMeta *meta;
+  uint32_t *key_rows;
+};
+
+// Launch helpers (return cudaError_t of the launch). `grid_ctas` = 0 picks the default
+// persistent grid (SM count x resident CTAs per SM).
+cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas = 0);
+cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream);
+cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream);
+cudaError_t launch_echo(const uint8_t *in, uint8_t *out, uint32_t n, cudaStream_t stream);
+
+// Host-side FNV-1a 32 (the same function the device probe computes).
+inline uint32_t fnv1a32(const uint8_t *key, uint32_t len) {
+  uint32_t h = 2166136261u;
+  for (uint32_t i = 0; i < len; ++i) {
+    h ^= key[i];
+    h *= 16777619u;
+  }
+  return h;
+}
+
+uint64_t kernel_launches();
+
+}  // namespace kvs

@@ -1,0 +1,1905 @@
+// kvs_runtime.cpp -- store shards, clients and the C ABI (include/kvs.h).
+//
+// Execution model
+//   * A shard (kvs_server) owns, on its GPU: the value slab (buddy heap of `unit_bytes` units),
+//     the device replica of the hash index (bucket words, entry metadata, key rows), and a
+//     write-through stream; on the host: the catalog (kvs::Directory) and the pinned host pool.
+//   * A client owns a CUDA stream on its GPU and a pinned/device staging area. Every call
+//     packs its metadata into the staging area, uploads it with one copy, and launches its
+//     kernels on the client stream. Work that touches a shard is ordered across clients by an
+//     event chain kept under the shard mutex: each call waits on the shard's last event before
+//     launching and records a new one after.
+//   * Host write-through is a device->host copy of each landed value on the shard's
+//     write-through stream, ordered after the gather by an event; the pending-host FIFO entry
+//     becomes committed at the next commit barrier (or earlier when allocation pressure forces
+//     it), exactly in issue order.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cerrno>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "kvs.h"
+#include "kvs_directory.hpp"
+#include "kvs_kernels.cuh"
+
+using kvs::Directory;
+using kvs::HostBacking;
+
+namespace {
+
+thread_local std::string g_err;
+
+int set_err(int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CUDA_TRY(x)                                                                          \
+  do {                                                                                       \
+    cudaError_t e_ = (x);                                                                    \
+    if (e_ != cudaSuccess) return set_err(KVS_E_CUDA, "%s failed: %s", #x, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define TRY(x)              \
+  do {                      \
+    int rc_ = (x);          \
+    if (rc_ != KVS_OK) return rc_; \
+  } while (0)
+
+uint64_t now_ns() {
+  return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Growable pinned host + device staging area. One upload per call.
+struct Staging {
+  uint8_t *host = nullptr;
+  uint8_t *dev = nullptr;
+  size_t cap = 0, used = 0;
+  cudaEvent_t uploaded = nullptr;  // last upload out of `host` finished
+
+  int init() {
+    CUDA_TRY(cudaEventCreateWithFlags(&uploaded, cudaEventDisableTiming));
+    return KVS_OK;
+  }
+  // Start packing a new call: waits until the previous upload has left `host`.
+  int begin(size_t need, cudaStream_t stream) {
+    CUDA_TRY(cudaEventSynchronize(uploaded));
+    used = 0;
+    if (need > cap) {
+      CUDA_TRY(cudaStreamSynchronize(stream));  // device staging may still be read
+      if (host) cudaFreeHost(host);
+      if (dev) cudaFree(dev);
+      host = nullptr;
+      dev = nullptr;
+      size_t c = std::max<size_t>(need, 1 << 20);
+      c = (c + 4095) & ~size_t(4095);
+      CUDA_TRY(cudaMallocHost(&host, c));
+      CUDA_TRY(cudaMalloc(&dev, c));
+      cap = c;
+    }
+    return KVS_OK;
+  }
+  // Reserve n bytes (16-byte aligned); returns the offset.
+  size_t take(size_t n) {
+    size_t off = (used + 15) & ~size_t(15);
+    used = off + n;
+    if (used > cap) {  // a sizing bug must never write past the buffer
+      std::fprintf(stderr, "kvs: staging overflow (%zu > %zu)\n", used, cap);
+      std::abort();
+    }
+    return off;
+  }
+  size_t push(const void *p, size_t n) {
+    size_t off = take(n);
+    if (n) std::memcpy(host + off, p, n);
+    return off;
+  }
+  template <class T> T *h(size_t off) { return reinterpret_cast<T *>(host + off); }
+  template <class T> T *d(size_t off) { return reinterpret_cast<T *>(dev + off); }
+  int upload(cudaStream_t stream, size_t bytes) {
+    if (bytes) CUDA_TRY(cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, stream));
+    CUDA_TRY(cudaEventRecord(uploaded, stream));
+    return KVS_OK;
+  }
+  void release() {
+    if (uploaded) cudaEventSynchronize(uploaded);
+    if (host) cudaFreeHost(host);
+    if (dev) cudaFree(dev);
+    if (uploaded) cudaEventDestroy(uploaded);
+    host = dev = nullptr;
+    uploaded = nullptr;
+    cap = used = 0;
+  }
+};
+
+uint64_t parse_env_u64(const char *name, uint64_t dflt, bool *bad) {
+  const char *v = std::getenv(name);
+  if (!v) return dflt;
+  // exact unsigned decimal, like the reference's parse_u64_exact (patch 0003 lines 5156-5260)
+  if (!*v) {
+    *bad = true;
+    return dflt;
+  }
+  uint64_t x = 0;
+  for (const char *p = v; *p; ++p) {
+    if (*p < '0' || *p > '9') {
+      *bad = true;
+      return dflt;
+    }
+    const uint64_t d = (uint64_t)(*p - '0');
+    if (x > (UINT64_MAX - d) / 10) {
+      *bad = true;
+      return dflt;
+    }
+    x = x * 10 + d;
+  }
+  return x;
+}
+
+}  // namespace
+
+// ============================================================================ shard
+
+struct WtBatch {
+  uint64_t id;
+  cudaEvent_t done;
+};
+
+struct kvs_server {
+  kvs_server_config cfg{};
+  std::mutex mu;
+  Directory *dir = nullptr;
+  uint8_t *slab = nullptr;
+  uint64_t *d_buckets = nullptr;
+  kvs::DevMeta *d_meta = nullptr;
+  uint32_t *d_keyrows = nullptr;
+  uint8_t *pool = nullptr;
+  cudaStream_t wt_stream = nullptr;
+  cudaEvent_t tail = nullptr;  // newest event of the shard's ordering chain (not owned)
+  std::vector<WtBatch> wt_batches;
+  std::vector<cudaEvent_t> free_events;
+  uint64_t next_batch = 1;
+  std::multimap<uint64_t, uint8_t *> heap_cache;  // recycled pinned buffers for off-pool values
+  std::atomic<uint64_t> moves_completed{0};
+  std::atomic<uint64_t> launches{0};
+  kvs_move_profile mprof{};
+  bool ready = false;
+  bool quarantined = false;
+
+  uint64_t slab_base() const { return reinterpret_cast<uint64_t>(slab); }
+
+  cudaEvent_t event_for_batch(uint64_t id) {
+    for (auto &b : wt_batches)
+      if (b.id == id) return b.done;
+    return nullptr;
+  }
+  int new_batch(uint64_t *id, cudaEvent_t *ev) {
+    cudaEvent_t e;
+    if (!free_events.empty()) {
+      e = free_events.back();
+      free_events.pop_back();
+    } else {
+      CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    *id = next_batch++;
+    wt_batches.push_back({*id, e});
+    *ev = e;
+    return KVS_OK;
+  }
+  void retire_batches() {
+    // a batch is retired once no FIFO entry refers to it
+    std::vector<WtBatch> keep;
+    for (auto &b : wt_batches) {
+      bool used = false;
+      for (auto &p : dir->fifo())
+        if ((uint64_t)p.wt_batch == b.id) {
+          used = true;
+          break;
+        }
+      if (used) keep.push_back(b); else free_events.push_back(b.done);
+    }
+    wt_batches.swap(keep);
+  }
+  uint8_t *host_ptr(const HostBacking &b) const {
+    return b.in_pool ? pool + b.pool_unit * cfg.unit_bytes : b.heap;
+  }
+  int reserve_backing(uint64_t len, HostBacking *out) {
+    HostBacking b;
+    b.present = true;
+    b.len = len;
+    uint64_t unit;
+    const uint64_t units = dir->units_for(len);
+    if (pool && dir->pool_alloc(units, &unit)) {
+      b.in_pool = true;
+      b.pool_unit = unit;
+      b.pool_units = units;
+    } else {
+      auto it = heap_cache.lower_bound(len);
+      if (it != heap_cache.end() && it->first <= 2 * len) {
+        b.heap = it->second;
+        heap_cache.erase(it);
+      } else {
+        void *p = nullptr;
+        CUDA_TRY(cudaHostAlloc(&p, len, cudaHostAllocPortable | cudaHostAllocMapped));
+        b.heap = (uint8_t *)p;
+      }
+      b.len = len;
+    }
+    *out = b;
+    return KVS_OK;
+  }
+  void release_backing(const HostBacking &b) {
+    if (!b.present) return;
+    if (b.in_pool)
+      dir->pool_release(b.pool_unit, b.pool_units);
+    else if (b.heap)
+      heap_cache.emplace(b.len, b.heap);
+  }
+  void release_dropped() {
+    for (auto &b : dir->take_dropped()) release_backing(b);
+  }
+  // Commit the FIFO head, waiting for its device->host copy.
+  int commit_one() {
+    auto &head = dir->fifo_head();
+    cudaEvent_t ev = event_for_batch((uint64_t)head.wt_batch);
+    const uint64_t t0 = now_ns();
+    if (ev) CUDA_TRY(cudaEventSynchronize(ev));
+    HostBacking released;
+    const uint64_t len = head.backing.len;
+    if (dir->commit_head(&released)) {
+      mprof.to_host_count++;
+      mprof.to_host_read_calls++;
+      mprof.to_host_read_bytes += len;
+      mprof.to_host_read_passes++;
+      mprof.to_host_device_pushes++;
+      const uint64_t dt = now_ns() - t0;
+      mprof.to_host_worker_ns += dt;
+      mprof.to_host_complete_ns += dt;
+      moves_completed.fetch_add(1, std::memory_order_relaxed);
+    } else {
+      release_backing(released);
+    }
+    return KVS_OK;
+  }
+  // COMMIT_BARRIER: every issued put becomes host-committed, in issue order.
+  int commit_all() {
+    if (dir->fifo_empty()) return KVS_OK;
+    cudaEvent_t last = event_for_batch((uint64_t)dir->fifo_back().wt_batch);
+    if (last) CUDA_TRY(cudaEventSynchronize(last));
+    while (!dir->fifo_empty()) TRY(commit_one());
+    retire_batches();
+    release_dropped();
+    return KVS_OK;
+  }
+};
+
+// ============================================================================ client
+
+struct kvs_client {
+  int device = 0;
+  std::vector<kvs_server *> shards;
+  std::mutex mu;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t entry_evt = nullptr, exit_evt = nullptr, landed_evt = nullptr;
+  std::vector<cudaEvent_t> chain_evt;  // per shard
+  Staging stage;
+  bool closed = false, quarantined = false;
+  kvs_put_profile prof{};
+  std::vector<uint64_t> validated_members;
+  // kernel timing (events around copy-engine launches)
+  bool timing = false;
+  struct Timed {
+    cudaEvent_t start, stop;
+    int kind;  // 0 gather, 1 scatter
+    uint64_t bytes;
+  };
+  std::vector<Timed> timed;
+  std::vector<cudaEvent_t> event_pool;
+  kvs_kernel_timing acc[2]{};
+  cudaEvent_t pooled_event() {
+    if (!event_pool.empty()) {
+      cudaEvent_t e = event_pool.back();
+      event_pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+  void time_begin(cudaEvent_t *start) {
+    *start = nullptr;
+    if (!timing) return;
+    *start = pooled_event();
+    cudaEventRecord(*start, stream);
+  }
+  void time_end(cudaEvent_t start, int kind, uint64_t bytes) {
+    if (!timing || !start) return;
+    cudaEvent_t stop = pooled_event();
+    cudaEventRecord(stop, stream);
+    timed.push_back({start, stop, kind, bytes});
+  }
+  void drain_timing() {
+    for (auto &t : timed) {
+      cudaEventSynchronize(t.stop);
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, t.start, t.stop);
+      acc[t.kind].launches++;
+      acc[t.kind].bytes += t.bytes;
+      acc[t.kind].total_ms += ms;
+      event_pool.push_back(t.start);
+      event_pool.push_back(t.stop);
+    }
+    timed.clear();
+  }
+};
+
+namespace {
+
+int check_client(kvs_client *c) {
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  if (c->closed) return set_err(KVS_E_CLOSED, "client is closed");
+  if (c->quarantined)
+    return set_err(KVS_E_QUARANTINED, "client is quarantined after an indeterminate failure");
+  return KVS_OK;
+}
+
+int validate_key(kvs_client *c, const void *key, uint32_t len, const char *op) {
+  if (len == 0) return set_err(KVS_E_INVAL, "%s: key must be non-empty", op);
+  uint32_t maxk = 128;
+  for (auto *s : c->shards) maxk = std::min(maxk, s->cfg.max_key_bytes);
+  if (len > maxk) return set_err(KVS_E_INVAL, "%s: key size %u exceeds Server max_key_bytes %u", op, len, maxk);
+  if (!key) return set_err(KVS_E_INVAL, "%s: key pointer is null", op);
+  return KVS_OK;
+}
+
+uint32_t shard_index(kvs_client *c, const uint8_t *key, uint32_t len) {
+  if (c->shards.size() == 1) return 0;
+  return kvs::fnv1a32(key, len) % (uint32_t)c->shards.size();
+}
+
+int check_device_ptr(kvs_client *c, const void *p, const char *op, const char *what) {
+  cudaPointerAttributes a{};
+  cudaError_t e = cudaPointerGetAttributes(&a, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(KVS_E_INVAL, "%s: %s must use DEVICE storage", op, what);
+  }
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+    return set_err(KVS_E_INVAL, "%s: %s must use DEVICE storage", op, what);
+  if (a.type == cudaMemoryTypeDevice && a.device != c->device)
+    return set_err(KVS_E_INVAL, "%s: %s must belong to the client device %d; got device %d", op, what,
+                   c->device, a.device);
+  return KVS_OK;
+}
+
+// Sorted, de-duplicated shard locks (get_parallel takes locks in address order, patch 0003
+// client_operations_adapter.cpp:145-187).
+struct ShardLocks {
+  std::vector<kvs_server *> held;
+  explicit ShardLocks(std::vector<kvs_server *> v) {
+    std::sort(v.begin(), v.end());
+    v.erase(std::unique(v.begin(), v.end()), v.end());
+    for (auto *s : v) s->mu.lock();
+    held = v;
+  }
+  ~ShardLocks() {
+    for (auto it = held.rbegin(); it != held.rend(); ++it) (*it)->mu.unlock();
+  }
+};
+
+int begin_op(kvs_client *c, void *caller) {
+  if (caller) {
+    CUDA_TRY(cudaEventRecord(c->entry_evt, (cudaStream_t)caller));
+    CUDA_TRY(cudaStreamWaitEvent(c->stream, c->entry_evt, 0));
+  }
+  return KVS_OK;
+}
+
+int end_op(kvs_client *c, void *caller) {
+  if (caller) {
+    CUDA_TRY(cudaEventRecord(c->exit_evt, c->stream));
+    CUDA_TRY(cudaStreamWaitEvent((cudaStream_t)caller, c->exit_evt, 0));
+  }
+  return KVS_OK;
+}
+
+int chain_wait(kvs_client *c, kvs_server *s) {
+  if (s->tail) CUDA_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
+  return KVS_OK;
+}
+
+int chain_record(kvs_client *c, size_t shard_idx) {
+  kvs_server *s = c->shards[shard_idx];
+  CUDA_TRY(cudaEventRecord(c->chain_evt[shard_idx], c->stream));
+  s->tail = c->chain_evt[shard_idx];
+  return KVS_OK;
+}
+
+// Mutations of one shard's index replica, packed into the staging area.
+struct PackedMutations {
+  size_t buckets_off = 0, meta_off = 0, keys_off = 0;
+  uint32_t nb = 0, nm = 0, nk = 0;
+};
+
+PackedMutations pack_mutations(kvs_server *s, Staging &st) {
+  PackedMutations pm;
+  auto buckets = s->dir->take_dirty_buckets();
+  auto slots = s->dir->take_dirty_slots();
+  auto keys = s->dir->take_dirty_keys();
+  pm.nb = (uint32_t)buckets.size();
+  pm.nm = (uint32_t)slots.size();
+  pm.nk = (uint32_t)keys.size();
+  pm.buckets_off = st.take(16ull * pm.nb);
+  uint64_t *bw = st.h<uint64_t>(pm.buckets_off);
+  for (size_t i = 0; i < buckets.size(); ++i) {
+    bw[2 * i] = buckets[i];
+    bw[2 * i + 1] = s->dir->bucket_word(buckets[i]);
+  }
+  pm.meta_off = st.take(24ull * pm.nm);
+  uint64_t *mw = st.h<uint64_t>(pm.meta_off);
+  for (size_t i = 0; i < slots.size(); ++i) {
+    const kvs::Entry &e = s->dir->entry(slots[i]);
+    kvs::DevMeta m{};
+    m.value_off = e.value_off;
+    m.total_len = (uint32_t)e.total_len;
+    m.valid = e.valid;
+    m.location = e.location;
+    m.key_len = e.key_len;
+    uint64_t words[2];
+    std::memcpy(words, &m, 16);
+    mw[3 * i] = slots[i];
+    mw[3 * i + 1] = words[0];
+    mw[3 * i + 2] = words[1];
+  }
+  pm.keys_off = st.take(4ull * (kvs::kKeyRowWords + 1) * pm.nk);
+  uint32_t *kw = st.h<uint32_t>(pm.keys_off);
+  for (size_t i = 0; i < keys.size(); ++i) {
+    uint32_t *rec = kw + i * (kvs::kKeyRowWords + 1);
+    rec[0] = keys[i];
+    std::memcpy(rec + 1, s->dir->entry(keys[i]).key, kvs::kMaxKeyBytes);
+  }
+  return pm;
+}
+
+// Exact staging bytes pack_mutations will take for the shard's current dirty sets.
+size_t mutation_upper_bound(kvs_server *s) {
+  size_t nb, nm, nk;
+  s->dir->dirty_counts(&nb, &nm, &nk);
+  return 16 * nb + 24 * nm + 4ull * (kvs::kKeyRowWords + 1) * nk + 64;
+}
+
+int launch_mutations(kvs_client *c, kvs_server *s, const PackedMutations &pm) {
+  kvs::MutationParams mp{};
+  mp.bucket_writes = c->stage.d<uint64_t>(pm.buckets_off);
+  mp.n_bucket_writes = pm.nb;
+  mp.meta_writes = c->stage.d<uint64_t>(pm.meta_off);
+  mp.n_meta_writes = pm.nm;
+  mp.key_writes = c->stage.d<uint32_t>(pm.keys_off);
+  mp.n_key_writes = pm.nk;
+  mp.buckets = s->d_buckets;
+  mp.meta = s->d_meta;
+  mp.key_rows = s->d_keyrows;
+  CUDA_TRY(kvs::launch_apply_mutations(mp, c->stream));
+  if (pm.nb + pm.nm + pm.nk) s->launches++;
+  return KVS_OK;
+}
+
+// Block value format for a layout: header words + region bases + value length.
+struct BlockFormat {
+  std::vector<uint32_t> header;
+  std::vector<uint64_t> region_bases;
+  std::vector<uint64_t> tile_prefix;
+  uint64_t value_len = 0;
+};
+
+constexpr uint32_t kTileBytes = 32 << 10;
+
+// Block value layout: header [MAGIC, n_layers, layer bytes...] zero padded to 32 bytes, then the
+// members back to back in member order, each member region starting on a 16-byte boundary (a
+// no-op for K/V blocks, whose sizes are multiples of 16; it aligns members such as 4-byte
+// per-block scales). Layer sizes in the header count the bytes the layer occupies.
+int block_format(const kvs_block_layout *L, BlockFormat *f) {
+  if (!L || L->n_members == 0 || !L->member_ptrs || !L->member_block_bytes)
+    return set_err(KVS_E_INVAL, "block layout: members must not be empty");
+  if (L->members_per_layer == 0 || L->n_members % L->members_per_layer)
+    return set_err(KVS_E_INVAL, "block layout: %u members is not a whole number of %u-member layers",
+                   L->n_members, L->members_per_layer);
+  const uint32_t n_layers = L->n_members / L->members_per_layer;
+  uint64_t hdr_words = 2 + n_layers;
+  hdr_words = (hdr_words + 7) / 8 * 8;
+  f->header.assign(hdr_words, 0);
+  f->header[0] = 0x524B564Eu;
+  f->header[1] = n_layers;
+  uint64_t off = 4 * hdr_words;
+  f->region_bases.resize(L->n_members);
+  f->tile_prefix.assign(L->n_members + 1, 0);
+  for (uint32_t m = 0; m < L->n_members; ++m) {
+    const uint64_t b = L->member_block_bytes[m];
+    if (b == 0 || b % 4)
+      return set_err(KVS_E_INVAL, "block layout: member %u block bytes %llu must be nonzero and 4-byte aligned", m,
+                     (unsigned long long)b);
+    if (!L->member_ptrs[m]) return set_err(KVS_E_INVAL, "block layout: member %u pointer is null", m);
+    const uint64_t start = off;
+    f->region_bases[m] = off;
+    off += b;
+    off = (off + 15) & ~uint64_t(15);
+    const uint32_t l = m / L->members_per_layer;
+    const uint64_t sz = (uint64_t)f->header[2 + l] + (off - start);
+    if (sz > 0xFFFFFFFFull) return set_err(KVS_E_INVAL, "block layout: layer %u exceeds the 32-bit header", l);
+    f->header[2 + l] = (uint32_t)sz;
+    f->tile_prefix[m + 1] = f->tile_prefix[m] + (b + kTileBytes - 1) / kTileBytes;
+  }
+  f->value_len = off;
+  return KVS_OK;
+}
+
+int validate_layout_ptrs(kvs_client *c, const kvs_block_layout *L, const char *op) {
+  std::vector<uint64_t> cur(L->member_ptrs, L->member_ptrs + L->n_members);
+  if (cur == c->validated_members) return KVS_OK;
+  for (uint32_t m = 0; m < L->n_members; ++m)
+    TRY(check_device_ptr(c, reinterpret_cast<const void *>(L->member_ptrs[m]), op, "member tensor"));
+  c->validated_members = cur;
+  return KVS_OK;
+}
+
+// ---------------------------------------------------------------------------- put machinery
+
+// One item staged for a put: the slab destination and either a block id (block puts) or a
+// source pointer and length (value puts).
+struct PutItem {
+  uint32_t shard;
+  uint64_t blob;     // absolute slab address
+  int64_t block_id;  // block puts
+  uint64_t src, len; // value puts
+  uint64_t slab_off;
+};
+
+struct PutBatch {
+  kvs_client *c;
+  const kvs_block_layout *layout;  // null for value puts
+  const BlockFormat *fmt;
+  std::vector<PutItem> items;
+  std::vector<uint8_t> involved;  // per shard
+};
+
+// Launch everything staged so far: replica mutations, the gather, and write-through.
+int flush_puts(PutBatch &b, cudaStream_t) {
+  kvs_client *c = b.c;
+  const size_t ns = c->shards.size();
+  bool any_dirty = false;
+  for (size_t i = 0; i < ns; ++i) any_dirty |= b.involved[i] != 0;
+  if (b.items.empty() && !any_dirty) return KVS_OK;
+  const uint64_t t0 = now_ns();
+  size_t need = 4096 + b.items.size() * 64;
+  if (b.layout) need += (size_t)b.layout->n_members * 40 + b.fmt->header.size() * 4;
+  for (size_t i = 0; i < ns; ++i)
+    if (b.involved[i]) need += mutation_upper_bound(c->shards[i]);
+  need += 64ull * b.items.size();
+  TRY(c->stage.begin(need, c->stream));
+  Staging &st = c->stage;
+  std::vector<PackedMutations> pms(ns);
+  for (size_t i = 0; i < ns; ++i)
+    if (b.involved[i]) pms[i] = pack_mutations(c->shards[i], st);
+  size_t blobs_off = 0, ids_off = 0, mp_off = 0, mb_off = 0, rb_off = 0, tp_off = 0, hw_off = 0;
+  const size_t n = b.items.size();
+  if (b.layout) {
+    blobs_off = st.take(8 * n);
+    ids_off = st.take(8 * n);
+    for (size_t i = 0; i < n; ++i) {
+      st.h<uint64_t>(blobs_off)[i] = b.items[i].blob;
+      st.h<int64_t>(ids_off)[i] = b.items[i].block_id;
+    }
+    mp_off = st.push(b.layout->member_ptrs, 8ull * b.layout->n_members);
+    mb_off = st.push(b.layout->member_block_bytes, 8ull * b.layout->n_members);
+    rb_off = st.push(b.fmt->region_bases.data(), 8ull * b.layout->n_members);
+    tp_off = st.push(b.fmt->tile_prefix.data(), 8ull * (b.layout->n_members + 1));
+    hw_off = st.push(b.fmt->header.data(), 4ull * b.fmt->header.size());
+  } else {
+    // value puts: per item {member ptr, bytes, region base 0, tile prefix 0..t, block 0, blob}
+    blobs_off = st.take(48 * n);
+    for (size_t i = 0; i < n; ++i) {
+      uint64_t *r = st.h<uint64_t>(blobs_off) + 6 * i;
+      r[0] = b.items[i].src;
+      r[1] = b.items[i].len;
+      r[2] = 0;
+      r[3] = 0;
+      r[4] = (b.items[i].len + kTileBytes - 1) / kTileBytes;
+      r[5] = b.items[i].blob;
+    }
+    ids_off = st.take(8);
+    *st.h<int64_t>(ids_off) = 0;
+  }
+  TRY(st.upload(c->stream, st.used));
+  for (size_t i = 0; i < ns; ++i)
+    if (b.involved[i]) TRY(chain_wait(c, c->shards[i]));
+  for (size_t i = 0; i < ns; ++i)
+    if (b.involved[i]) TRY(launch_mutations(c, c->shards[i], pms[i]));
+  if (n) {
+    if (b.layout) {
+      kvs::ChunkCopyParams p{};
+      p.member_ptrs = st.d<uint64_t>(mp_off);
+      p.member_bytes = st.d<uint64_t>(mb_off);
+      p.region_bases = st.d<uint64_t>(rb_off);
+      p.tile_prefix = st.d<uint64_t>(tp_off);
+      p.block_ids = st.d<int64_t>(ids_off);
+      p.blob_ptrs = st.d<uint64_t>(blobs_off);
+      p.header_words = st.d<uint32_t>(hw_off);
+      p.n_header_words = (uint32_t)b.fmt->header.size();
+      p.n_blobs = (uint32_t)n;
+      p.blocks_per_blob = 1;
+      p.n_ranks = 1;
+      p.n_members = b.layout->n_members;
+      p.tile_bytes = kTileBytes;
+      p.tiles_per_combo = b.fmt->tile_prefix.back();
+      p.total_tiles = (uint64_t)n * p.tiles_per_combo;
+      p.to_blob = 1;
+      cudaEvent_t t0 = nullptr;
+      c->time_begin(&t0);
+      CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+      c->time_end(t0, 0, (uint64_t)n * (b.fmt->value_len - 4ull * b.fmt->header.size()));
+    } else {
+      for (size_t i = 0; i < n; ++i) {
+        const size_t r = blobs_off + 48 * i;
+        kvs::ChunkCopyParams p{};
+        p.member_ptrs = st.d<uint64_t>(r);
+        p.member_bytes = st.d<uint64_t>(r + 8);
+        p.region_bases = st.d<uint64_t>(r + 16);
+        p.tile_prefix = st.d<uint64_t>(r + 24);
+        p.block_ids = st.d<int64_t>(ids_off);
+        p.blob_ptrs = st.d<uint64_t>(r + 40);
+        p.n_blobs = 1;
+        p.blocks_per_blob = 1;
+        p.n_ranks = 1;
+        p.n_members = 1;
+        p.tile_bytes = kTileBytes;
+        p.tiles_per_combo = (b.items[i].len + kTileBytes - 1) / kTileBytes;
+        p.total_tiles = p.tiles_per_combo;
+        p.to_blob = 1;
+        CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+      }
+    }
+    for (size_t i = 0; i < ns; ++i)
+      if (b.involved[i]) c->shards[i]->launches += b.layout ? 1 : n;
+  }
+  CUDA_TRY(cudaEventRecord(c->landed_evt, c->stream));
+  for (size_t i = 0; i < ns; ++i)
+    if (b.involved[i]) TRY(chain_record(c, i));
+  const uint64_t t1 = now_ns();
+  // write-through: one device->host copy per value on each shard's write-through stream
+  std::vector<size_t> per_shard(ns, 0);
+  for (auto &it : b.items) per_shard[it.shard]++;
+  for (size_t si = 0; si < ns; ++si) {
+    if (!per_shard[si]) continue;
+    kvs_server *s = c->shards[si];
+    DeviceGuard g(s->cfg.device);
+    CUDA_TRY(cudaStreamWaitEvent(s->wt_stream, c->landed_evt, 0));
+    uint64_t batch_id = 0;
+    cudaEvent_t ev = nullptr;
+    TRY(s->new_batch(&batch_id, &ev));
+    auto &fifo = s->dir->fifo();
+    size_t k = fifo.size() - per_shard[si];
+    for (auto &it : b.items) {
+      if (it.shard != si) continue;
+      kvs::PendingPut &pp = fifo[k++];
+      const uint64_t len = s->dir->entry(pp.slot).total_len;
+      TRY(s->reserve_backing(len, &pp.backing));
+      pp.wt_batch = (int)batch_id;
+      CUDA_TRY(cudaMemcpyAsync(s->host_ptr(pp.backing), s->slab + it.slab_off, len, cudaMemcpyDeviceToHost,
+                               s->wt_stream));
+    }
+    CUDA_TRY(cudaEventRecord(ev, s->wt_stream));
+  }
+  c->prof.program_ns += t1 - t0;
+  c->prof.enqueue_ns += now_ns() - t1;
+  b.items.clear();
+  return KVS_OK;
+}
+
+// Stage one put; drives forced commits when a pending entry blocks it.
+int stage_put(PutBatch &b, uint32_t si, const uint8_t *key, uint32_t key_len, uint64_t value_len,
+              int64_t block_id, uint64_t src) {
+  kvs_server *s = b.c->shards[si];
+  b.involved[si] = 1;
+  for (;;) {
+    kvs::Grant g;
+    const kvs::Prepare r = s->dir->prepare_put(key, key_len, value_len, &g);
+    if (r == kvs::Prepare::kGranted) {
+      b.items.push_back(PutItem{si, s->slab_base() + g.value_off, block_id, src, value_len, g.value_off});
+      return KVS_OK;
+    }
+    TRY(flush_puts(b, b.c->stream));
+    if (r == kvs::Prepare::kNoSpace)
+      return set_err(KVS_E_NOSPACE, "put: no device-cache space for a %llu B value", (unsigned long long)value_len);
+    TRY(s->commit_one());  // force_put_host_commit, then retry the prepare
+    s->retire_batches();
+    s->release_dropped();
+  }
+}
+
+int commit_barrier(kvs_client *c, const std::vector<uint8_t> &involved) {
+  for (size_t i = 0; i < c->shards.size(); ++i)
+    if (involved[i]) TRY(c->shards[i]->commit_all());
+  return KVS_OK;
+}
+
+std::vector<kvs_server *> involved_servers(kvs_client *c, const std::vector<uint8_t> &inv) {
+  std::vector<kvs_server *> v;
+  for (size_t i = 0; i < c->shards.size(); ++i)
+    if (inv[i]) v.push_back(c->shards[i]);
+  return v;
+}
+
+int quarantine_on_error(kvs_client *c, int rc) {
+  if (rc == KVS_E_CUDA) c->quarantined = true;
+  return rc;
+}
+
+// Copy one value between a slab location and a buffer with the copy engine kernel.
+int launch_value_copy(kvs_client *c, uint64_t dst, uint64_t src, uint64_t len, size_t rec_off) {
+  // rec layout: {member ptr(dst buffer), bytes, region base 0, tile prefix[2], blob ptr(src)}
+  uint64_t *r = c->stage.h<uint64_t>(rec_off);
+  (void)r;
+  kvs::ChunkCopyParams p{};
+  p.member_ptrs = c->stage.d<uint64_t>(rec_off);
+  p.member_bytes = c->stage.d<uint64_t>(rec_off + 8);
+  p.region_bases = c->stage.d<uint64_t>(rec_off + 16);
+  p.tile_prefix = c->stage.d<uint64_t>(rec_off + 24);
+  p.block_ids = c->stage.d<int64_t>(rec_off + 48);
+  p.blob_ptrs = c->stage.d<uint64_t>(rec_off + 40);
+  p.n_blobs = 1;
+  p.blocks_per_blob = 1;
+  p.n_ranks = 1;
+  p.n_members = 1;
+  p.tile_bytes = kTileBytes;
+  p.tiles_per_combo = (len + kTileBytes - 1) / kTileBytes;
+  p.total_tiles = p.tiles_per_combo;
+  p.to_blob = 0;
+  (void)dst;
+  (void)src;
+  CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+  return KVS_OK;
+}
+
+size_t stage_value_copy(Staging &st, uint64_t dst, uint64_t src, uint64_t len) {
+  const size_t off = st.take(56);
+  uint64_t *r = st.h<uint64_t>(off);
+  r[0] = dst;
+  r[1] = len;
+  r[2] = 0;
+  r[3] = 0;
+  r[4] = (len + kTileBytes - 1) / kTileBytes;
+  r[5] = src;
+  r[6] = 0;  // block id
+  return off;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+
+extern "C" {
+
+int kvs_abi_version(void) { return KVS_ABI_VERSION; }
+
+const char *kvs_last_error(void) { return g_err.c_str(); }
+
+uint64_t kvs_kernel_launch_count(void) { return kvs::kernel_launches(); }
+
+int kvs_server_config_default(kvs_server_config *cfg) {
+  if (!cfg) return set_err(KVS_E_INVAL, "config is null");
+  std::memset(cfg, 0, sizeof *cfg);
+  bool bad = false;
+  cfg->device = 0;
+  cfg->max_keys = (uint32_t)parse_env_u64("KVM_SERVER_DRAM_MAX_KEYS", 1024, &bad);
+  if (bad) return set_err(KVS_E_INVAL, "KVM_SERVER_DRAM_MAX_KEYS must be an unsigned decimal integer");
+  cfg->heap_bytes = parse_env_u64("KVM_SERVER_DRAM_VALUE_HEAP_BYTES", 1434541824ull, &bad);
+  if (bad) return set_err(KVS_E_INVAL, "KVM_SERVER_DRAM_VALUE_HEAP_BYTES must be an unsigned decimal integer");
+  cfg->host_pool_bytes = parse_env_u64("KVM_SERVER_HOST_POOL_BYTES", 1ull << 30, &bad);
+  if (bad) return set_err(KVS_E_INVAL, "KVM_SERVER_HOST_POOL_BYTES must be an unsigned decimal integer");
+  cfg->max_value_bytes = parse_env_u64("KVM_COMMON_MAX_VALUE_BYTES", 64ull << 20, &bad);
+  if (bad) return set_err(KVS_E_INVAL, "KVM_COMMON_MAX_VALUE_BYTES must be an unsigned decimal integer");
+  cfg->max_key_bytes = (uint32_t)parse_env_u64("KVM_SERVER_MAX_KEY_BYTES", 128, &bad);
+  if (bad) return set_err(KVS_E_INVAL, "KVM_SERVER_MAX_KEY_BYTES must be an unsigned decimal integer");
+  cfg->unit_bytes = 4288;
+  if (cfg->max_keys == 0 || cfg->max_keys > (1u << 26))
+    return set_err(KVS_E_INVAL, "KVM_SERVER_DRAM_MAX_KEYS must be in 1..67108864");
+  if (cfg->max_key_bytes == 0 || cfg->max_key_bytes > 128)
+    return set_err(KVS_E_INVAL, "KVM_SERVER_MAX_KEY_BYTES must be in 1..128");
+  if (cfg->max_value_bytes == 0) return set_err(KVS_E_INVAL, "KVM_COMMON_MAX_VALUE_BYTES must be > 0");
+  return KVS_OK;
+}
+
+int kvs_server_create(const kvs_server_config *cfg_in, kvs_server **out) {
+  if (!cfg_in || !out) return set_err(KVS_E_INVAL, "config and out must be non-null");
+  *out = nullptr;
+  kvs_server_config cfg = *cfg_in;
+  if (cfg.unit_bytes == 0) cfg.unit_bytes = 4288;
+  if (cfg.max_key_bytes == 0) cfg.max_key_bytes = 128;
+  if (cfg.max_value_bytes == 0) cfg.max_value_bytes = 64ull << 20;
+  if (cfg.max_keys == 0) return set_err(KVS_E_INVAL, "max_keys must be > 0");
+  if (cfg.unit_bytes % 16) return set_err(KVS_E_INVAL, "unit_bytes must be a multiple of 16");
+  if (cfg.max_key_bytes > 128) return set_err(KVS_E_INVAL, "max_key_bytes must be <= 128");
+  if (cfg.heap_bytes < cfg.unit_bytes) return set_err(KVS_E_INVAL, "value heap smaller than one unit");
+  if (cfg.heap_bytes / cfg.unit_bytes > 0xFFFFFFF0ull) return set_err(KVS_E_INVAL, "value heap has too many units");
+  int ndev = 0;
+  CUDA_TRY(cudaGetDeviceCount(&ndev));
+  if (cfg.device < 0 || cfg.device >= ndev)
+    return set_err(KVS_E_INVAL, "device %d is not a visible CUDA device (%d visible)", cfg.device, ndev);
+  auto *s = new (std::nothrow) kvs_server();
+  if (!s) return set_err(KVS_E_NOSPACE, "out of host memory");
+  s->cfg = cfg;
+  DeviceGuard g(cfg.device);
+  auto fail = [&](int rc) {
+    kvs_server_destroy(s);
+    return rc;
+  };
+  try {
+    kvs::DirConfig dc{cfg.max_keys, cfg.unit_bytes, cfg.max_key_bytes, cfg.heap_bytes, cfg.max_value_bytes,
+                      cfg.host_pool_bytes / cfg.unit_bytes};
+    s->dir = new Directory(dc);
+  } catch (const std::exception &e) {
+    return fail(set_err(KVS_E_INVAL, "server config: %s", e.what()));
+  }
+  cudaError_t e;
+  if ((e = cudaMalloc(&s->slab, cfg.heap_bytes)) != cudaSuccess)
+    return fail(set_err(KVS_E_NOSPACE, "slab of %llu B: %s", (unsigned long long)cfg.heap_bytes, cudaGetErrorString(e)));
+  const uint32_t nb = s->dir->num_buckets();
+  if ((e = cudaMalloc(&s->d_buckets, 8ull * nb)) != cudaSuccess ||
+      (e = cudaMalloc(&s->d_meta, sizeof(kvs::DevMeta) * cfg.max_keys)) != cudaSuccess ||
+      (e = cudaMalloc(&s->d_keyrows, 4ull * kvs::kKeyRowWords * cfg.max_keys)) != cudaSuccess)
+    return fail(set_err(KVS_E_NOSPACE, "index replica: %s", cudaGetErrorString(e)));
+  // empty buckets are all-ones; metadata and key rows start zeroed
+  if ((e = cudaMemset(s->d_buckets, 0xFF, 8ull * nb)) != cudaSuccess ||
+      (e = cudaMemset(s->d_meta, 0, sizeof(kvs::DevMeta) * cfg.max_keys)) != cudaSuccess ||
+      (e = cudaMemset(s->d_keyrows, 0, 4ull * kvs::kKeyRowWords * cfg.max_keys)) != cudaSuccess)
+    return fail(set_err(KVS_E_CUDA, "index replica init: %s", cudaGetErrorString(e)));
+  // the replica words are {hash, slot}: an empty bucket has slot 0xFFFFFFFF; hash is don't-care
+  if (cfg.host_pool_bytes / cfg.unit_bytes) {
+    const uint64_t bytes = (cfg.host_pool_bytes / cfg.unit_bytes) * cfg.unit_bytes;
+    if ((e = cudaHostAlloc(&s->pool, bytes, cudaHostAllocPortable | cudaHostAllocMapped)) != cudaSuccess)
+      return fail(set_err(KVS_E_NOSPACE, "host pool of %llu B: %s", (unsigned long long)bytes, cudaGetErrorString(e)));
+  }
+  if ((e = cudaStreamCreateWithFlags(&s->wt_stream, cudaStreamNonBlocking)) != cudaSuccess)
+    return fail(set_err(KVS_E_CUDA, "write-through stream: %s", cudaGetErrorString(e)));
+  if ((e = cudaDeviceSynchronize()) != cudaSuccess)
+    return fail(set_err(KVS_E_CUDA, "server init: %s", cudaGetErrorString(e)));
+  s->ready = true;
+  *out = s;
+  return KVS_OK;
+}
+
+int kvs_server_destroy(kvs_server *s) {
+  if (!s) return KVS_OK;
+  int rc = KVS_OK;
+  {
+    std::lock_guard<std::mutex> lk(s->mu);
+    DeviceGuard g(s->cfg.device);
+    if (s->dir && s->wt_stream) {
+      cudaStreamSynchronize(s->wt_stream);
+      if (!s->dir->fifo_empty()) rc = s->commit_all();
+    }
+    if (s->wt_stream) cudaStreamSynchronize(s->wt_stream);
+    for (auto &b : s->wt_batches) cudaEventDestroy(b.done);
+    for (auto e : s->free_events) cudaEventDestroy(e);
+    if (s->dir) {
+      for (uint32_t i = 0; i < s->cfg.max_keys; ++i) {
+        HostBacking &hb = s->dir->backing(i);
+        if (hb.present && !hb.in_pool && hb.heap) cudaFreeHost(hb.heap);
+      }
+      for (auto &p : s->dir->fifo())
+        if (p.backing.present && !p.backing.in_pool && p.backing.heap) cudaFreeHost(p.backing.heap);
+      for (auto &b : s->dir->take_dropped())
+        if (!b.in_pool && b.heap) cudaFreeHost(b.heap);
+    }
+    for (auto &kv : s->heap_cache) cudaFreeHost(kv.second);
+    if (s->wt_stream) cudaStreamDestroy(s->wt_stream);
+    if (s->pool) cudaFreeHost(s->pool);
+    if (s->d_keyrows) cudaFree(s->d_keyrows);
+    if (s->d_meta) cudaFree(s->d_meta);
+    if (s->d_buckets) cudaFree(s->d_buckets);
+    if (s->slab) cudaFree(s->slab);
+    delete s->dir;
+  }
+  delete s;
+  return rc;
+}
+
+int kvs_server_is_ready(kvs_server *s, int *ready) {
+  if (!s || !ready) return set_err(KVS_E_INVAL, "null argument");
+  *ready = s->ready && !s->quarantined;
+  return KVS_OK;
+}
+
+int kvs_server_moves_completed(kvs_server *s, uint64_t *out) {
+  if (!s || !out) return set_err(KVS_E_INVAL, "null argument");
+  *out = s->moves_completed.load();
+  return KVS_OK;
+}
+
+int kvs_server_move_profile(kvs_server *s, kvs_move_profile *out) {
+  if (!s || !out) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  *out = s->mprof;
+  return KVS_OK;
+}
+
+int kvs_server_allocator_profile(kvs_server *s, kvs_allocator_profile *out) {
+  if (!s || !out) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  std::memset(out, 0, sizeof *out);
+  auto &st = s->dir->stats();
+  out->allocation_calls = st.allocation_calls;
+  out->allocation_successes = st.allocation_successes;
+  out->allocation_failures = st.allocation_failures;
+  out->victim_scans = st.victim_scans;
+  out->victims_evicted = st.victims_evicted;
+  return KVS_OK;
+}
+
+int kvs_server_stats(kvs_server *s, kvs_stats *out) {
+  if (!s || !out) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  std::memset(out, 0, sizeof *out);
+  auto &st = s->dir->stats();
+  out->live_device_bytes = s->dir->live_device_bytes();
+  out->pending_device_bytes = s->dir->pending_device_bytes();
+  out->live_keys = s->dir->live_keys(&out->device_resident_keys);
+  out->allocation_calls = st.allocation_calls;
+  out->allocation_successes = st.allocation_successes;
+  out->allocation_failures = st.allocation_failures;
+  out->victims_evicted = st.victims_evicted;
+  out->catalog_replacements = st.catalog_replacements;
+  out->writes_through = st.writes_through;
+  out->stale_commits = st.stale_commits;
+  out->host_serves = st.host_serves;
+  out->admissions = st.admissions;
+  out->pool_values = st.pool_values;
+  out->heap_values = st.heap_values;
+  out->epoch = s->dir->epoch();
+  out->issued = st.issued;
+  out->committed = st.committed;
+  out->kernel_launches = s->launches.load();
+  return KVS_OK;
+}
+
+int kvs_server_device(kvs_server *s, int *device) {
+  if (!s || !device) return set_err(KVS_E_INVAL, "null argument");
+  *device = s->cfg.device;
+  return KVS_OK;
+}
+
+int kvs_server_put_drain_progress(kvs_server *s, uint32_t *issued, uint32_t *committed) {
+  if (!s || !issued || !committed) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  *issued = s->dir->stats().issued;
+  *committed = s->dir->stats().committed;
+  return KVS_OK;
+}
+
+int kvs_server_location(kvs_server *s, const void *key, uint32_t key_len, int *location, uint64_t *value_off) {
+  if (!s || !key || !location) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  const uint32_t slot = s->dir->lookup((const uint8_t *)key, key_len);
+  if (slot == kvs::kBucketEmpty) {
+    *location = KVS_LOC_ABSENT;
+    return KVS_OK;
+  }
+  *location = s->dir->entry(slot).location;
+  if (value_off) *value_off = s->dir->entry(slot).value_off;
+  return KVS_OK;
+}
+
+int kvs_server_index_snapshot(kvs_server *s, uint32_t *host_pairs, uint32_t *device_pairs, uint32_t cap_pairs,
+                              uint32_t *n_buckets) {
+  if (!s || !n_buckets) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  const uint32_t nb = s->dir->num_buckets();
+  *n_buckets = nb;
+  if (cap_pairs < nb) return KVS_OK;
+  DeviceGuard g(s->cfg.device);
+  if (s->tail) CUDA_TRY(cudaEventSynchronize(s->tail));
+  if (host_pairs) std::memcpy(host_pairs, s->dir->bucket_pairs(), 8ull * nb);
+  if (device_pairs) {
+    std::vector<uint64_t> w(nb);
+    CUDA_TRY(cudaMemcpy(w.data(), s->d_buckets, 8ull * nb, cudaMemcpyDeviceToHost));
+    for (uint32_t b = 0; b < nb; ++b) {
+      device_pairs[2 * b] = (uint32_t)w[b];
+      device_pairs[2 * b + 1] = (uint32_t)(w[b] >> 32);
+    }
+  }
+  return KVS_OK;
+}
+
+int kvs_server_lru_order(kvs_server *s, uint32_t *slots, uint32_t cap, uint32_t *n) {
+  if (!s || !n) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  *n = s->dir->lru_order(slots, slots ? cap : 0);
+  return KVS_OK;
+}
+
+// ---------------------------------------------------------------------------- client
+
+int kvs_client_create(kvs_server *const *shards, uint32_t n_shards, int32_t device, kvs_client **out) {
+  if (!out) return set_err(KVS_E_INVAL, "out is null");
+  *out = nullptr;
+  if (!shards || n_shards == 0) return set_err(KVS_E_INVAL, "a client needs at least one server shard");
+  int ndev = 0;
+  CUDA_TRY(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_err(KVS_E_INVAL, "device %d is not a visible CUDA device", device);
+  for (uint32_t i = 0; i < n_shards; ++i)
+    if (!shards[i]) return set_err(KVS_E_INVAL, "shard %u is null", i);
+  auto *c = new (std::nothrow) kvs_client();
+  if (!c) return set_err(KVS_E_NOSPACE, "out of host memory");
+  c->device = device;
+  c->shards.assign(shards, shards + n_shards);
+  DeviceGuard g(device);
+  // peer access to every remote shard's GPU: put / get kernels store and load over NVLink
+  for (auto *s : c->shards) {
+    if (s->cfg.device == device) continue;
+    int can = 0;
+    CUDA_TRY(cudaDeviceCanAccessPeer(&can, device, s->cfg.device));
+    if (!can) {
+      delete c;
+      return set_err(KVS_E_INVAL, "device %d cannot access peer device %d", device, s->cfg.device);
+    }
+    cudaError_t e = cudaDeviceEnablePeerAccess(s->cfg.device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+    else if (e != cudaSuccess) {
+      delete c;
+      return set_err(KVS_E_CUDA, "enable peer access %d->%d: %s", device, s->cfg.device, cudaGetErrorString(e));
+    }
+  }
+  cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->entry_evt, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->exit_evt, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->landed_evt, cudaEventDisableTiming);
+  c->chain_evt.assign(n_shards, nullptr);
+  for (uint32_t i = 0; i < n_shards && e == cudaSuccess; ++i)
+    e = cudaEventCreateWithFlags(&c->chain_evt[i], cudaEventDisableTiming);
+  if (e != cudaSuccess || c->stage.init() != KVS_OK) {
+    kvs_client_destroy(c);
+    return set_err(KVS_E_CUDA, "client init: %s", cudaGetErrorString(e));
+  }
+  *out = c;
+  return KVS_OK;
+}
+
+int kvs_client_destroy(kvs_client *c) {
+  if (!c) return KVS_OK;
+  int rc = KVS_OK;
+  {
+    std::lock_guard<std::mutex> lk(c->mu);
+    DeviceGuard g(c->device);
+    if (!c->closed && !c->quarantined && c->stream) {
+      // drain every issued put of this client's shards (Client::close, design.md section 8)
+      std::vector<uint8_t> inv(c->shards.size(), 1);
+      ShardLocks locks(involved_servers(c, inv));
+      rc = commit_barrier(c, inv);
+      cudaStreamSynchronize(c->stream);
+      for (size_t i = 0; i < c->shards.size(); ++i)
+        if (c->shards[i]->tail == c->chain_evt[i]) {
+          // keep the chain valid: hand the shard a completed chain position
+          c->shards[i]->tail = nullptr;
+        }
+    } else if (c->stream) {
+      cudaStreamSynchronize(c->stream);
+      std::vector<kvs_server *> all(c->shards);
+      ShardLocks locks(all);
+      for (size_t i = 0; i < c->shards.size(); ++i)
+        if (c->shards[i]->tail == c->chain_evt[i]) c->shards[i]->tail = nullptr;
+    }
+    c->closed = true;
+    c->drain_timing();
+    for (auto e : c->event_pool) cudaEventDestroy(e);
+    c->stage.release();
+    for (auto e : c->chain_evt)
+      if (e) cudaEventDestroy(e);
+    if (c->entry_evt) cudaEventDestroy(c->entry_evt);
+    if (c->exit_evt) cudaEventDestroy(c->exit_evt);
+    if (c->landed_evt) cudaEventDestroy(c->landed_evt);
+    if (c->stream) cudaStreamDestroy(c->stream);
+  }
+  delete c;
+  return rc;
+}
+
+int kvs_client_is_established(kvs_client *c, int *established) {
+  if (!c || !established) return set_err(KVS_E_INVAL, "null argument");
+  *established = !c->closed && !c->quarantined;
+  return KVS_OK;
+}
+
+int kvs_client_shard_of(kvs_client *c, const void *key, uint32_t key_len, uint32_t *shard) {
+  if (!c || !key || !shard) return set_err(KVS_E_INVAL, "null argument");
+  *shard = shard_index(c, (const uint8_t *)key, key_len);
+  return KVS_OK;
+}
+
+int kvs_client_put_profile(kvs_client *c, kvs_put_profile *out) {
+  if (!c || !out) return set_err(KVS_E_INVAL, "null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  *out = c->prof;
+  return KVS_OK;
+}
+
+int kvs_ping(kvs_client *c, const void *payload, uint32_t len, void *out, void *stream) {
+  TRY(check_client(c));
+  if (len > 1024) return set_err(KVS_E_INVAL, "ping: payload of %u bytes exceeds the 1024-byte limit", len);
+  if (len && (!payload || !out)) return set_err(KVS_E_INVAL, "ping: null payload or output");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(begin_op(c, stream));
+  TRY(c->stage.begin(4096, c->stream));
+  const size_t in_off = c->stage.push(payload, len);
+  const size_t out_off = c->stage.take(len);
+  TRY(c->stage.upload(c->stream, c->stage.used));
+  CUDA_TRY(kvs::launch_echo(c->stage.d<uint8_t>(in_off), c->stage.d<uint8_t>(out_off), len, c->stream));
+  if (len) CUDA_TRY(cudaMemcpyAsync(out, c->stage.d<uint8_t>(out_off), len, cudaMemcpyDeviceToHost, c->stream));
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  TRY(end_op(c, stream));
+  return KVS_OK;
+}
+
+static int put_values(kvs_client *c, uint32_t n, const void *const *keys, const uint32_t *key_lens,
+                      const void *const *values, const uint64_t *value_lens, int sync_commit, void *stream,
+                      const char *op) {
+  TRY(check_client(c));
+  if (n && (!keys || !key_lens || !values || !value_lens)) return set_err(KVS_E_INVAL, "%s: null argument", op);
+  const uint64_t t0 = now_ns();
+  for (uint32_t i = 0; i < n; ++i) {
+    TRY(validate_key(c, keys[i], key_lens[i], op));
+    if (value_lens[i] == 0) return set_err(KVS_E_INVAL, "%s: value_len_bytes must be > 0", op);
+    for (auto *s : c->shards)
+      if (value_lens[i] > s->cfg.max_value_bytes)
+        return set_err(KVS_E_INVAL, "%s: value_len_bytes %llu exceeds max_value_bytes %llu", op,
+                       (unsigned long long)value_lens[i], (unsigned long long)s->cfg.max_value_bytes);
+  }
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  for (uint32_t i = 0; i < n; ++i) TRY(check_device_ptr(c, values[i], op, "tensor"));
+  std::vector<uint8_t> inv(c->shards.size(), 0);
+  std::vector<uint32_t> si(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    si[i] = shard_index(c, (const uint8_t *)keys[i], key_lens[i]);
+    inv[si[i]] = 1;
+  }
+  ShardLocks locks(involved_servers(c, inv));
+  TRY(begin_op(c, stream));
+  PutBatch b{c, nullptr, nullptr, {}, std::vector<uint8_t>(c->shards.size(), 0)};
+  const uint64_t t1 = now_ns();
+  for (uint32_t i = 0; i < n; ++i)
+    TRY(quarantine_on_error(c, stage_put(b, si[i], (const uint8_t *)keys[i], key_lens[i], value_lens[i], 0,
+                                         reinterpret_cast<uint64_t>(values[i]))));
+  c->prof.prepare_ns += now_ns() - t1;
+  TRY(quarantine_on_error(c, flush_puts(b, c->stream)));
+  const uint64_t t2 = now_ns();
+  if (sync_commit) TRY(quarantine_on_error(c, commit_barrier(c, inv)));
+  c->prof.commit_wait_ns += now_ns() - t2;
+  TRY(end_op(c, stream));
+  c->prof.count += n;
+  c->prof.total_ns += now_ns() - t0;
+  return KVS_OK;
+}
+
+int kvs_put(kvs_client *c, const void *key, uint32_t key_len, const void *value, uint64_t value_len,
+            int sync_commit, void *stream) {
+  return put_values(c, 1, &key, &key_len, &value, &value_len, sync_commit, stream, "put");
+}
+
+int kvs_put_batch(kvs_client *c, uint32_t n, const void *const *keys, const uint32_t *key_lens,
+                  const void *const *values, const uint64_t *value_lens, int sync_commit, void *stream) {
+  if (n > 128) return set_err(KVS_E_INVAL, "put_batch: %u items exceed the 128-descriptor limit", n);
+  return put_values(c, n, keys, key_lens, values, value_lens, sync_commit, stream, "put_batch");
+}
+
+int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_t capacity, int *found,
+            uint64_t *value_len, void *stream) {
+  TRY(check_client(c));
+  if (!found) return set_err(KVS_E_INVAL, "get: found is null");
+  *found = 0;
+  TRY(validate_key(c, key, key_len, "get"));
+  if (capacity == 0) return set_err(KVS_E_INVAL, "get: out_tensor packed byte size must be > 0");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(check_device_ptr(c, out, "get", "tensor"));
+  const uint32_t si = shard_index(c, (const uint8_t *)key, key_len);
+  kvs_server *s = c->shards[si];
+  std::lock_guard<std::mutex> sl(s->mu);
+  TRY(quarantine_on_error(c, s->commit_all()));  // GET preserves host-commit ordering first
+  const uint32_t slot = s->dir->lookup((const uint8_t *)key, key_len);
+  if (slot == kvs::kBucketEmpty) return KVS_OK;
+  const kvs::Entry &e = s->dir->entry(slot);
+  if (value_len) *value_len = e.total_len;
+  if (e.total_len > capacity)
+    return set_err(KVS_E_TOO_SMALL, "get: out_tensor packed capacity %llu is smaller than the stored value",
+                   (unsigned long long)capacity);
+  uint64_t admit_off = 0;
+  const auto action = s->dir->get_hit(slot, &admit_off);
+  const HostBacking &hb = s->dir->backing(slot);
+  const uint64_t len = e.total_len;
+  TRY(begin_op(c, stream));
+  TRY(c->stage.begin(4096 + mutation_upper_bound(s), c->stream));
+  PackedMutations pm = pack_mutations(s, c->stage);
+  uint64_t src;
+  if (action == Directory::GetAction::kHostOnly)
+    src = reinterpret_cast<uint64_t>(s->host_ptr(hb));  // mapped pinned memory, read over PCIe
+  else
+    src = s->slab_base() + e.value_off;
+  const size_t rec = stage_value_copy(c->stage, reinterpret_cast<uint64_t>(out), src, len);
+  TRY(c->stage.upload(c->stream, c->stage.used));
+  TRY(chain_wait(c, s));
+  TRY(quarantine_on_error(c, launch_mutations(c, s, pm)));
+  if (action == Directory::GetAction::kAdmit)
+    CUDA_TRY(cudaMemcpyAsync(s->slab + admit_off, s->host_ptr(hb), len, cudaMemcpyHostToDevice, c->stream));
+  TRY(quarantine_on_error(c, launch_value_copy(c, 0, 0, len, rec)));
+  s->launches++;
+  TRY(chain_record(c, si));
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  if (action != Directory::GetAction::kDevice) {
+    s->mprof.to_device_count++;
+    s->moves_completed.fetch_add(1, std::memory_order_relaxed);
+  }
+  TRY(end_op(c, stream));
+  *found = 1;
+  return KVS_OK;
+}
+
+int kvs_get_parallel(kvs_client *const *clients, uint32_t n, const void *const *keys, const uint32_t *key_lens,
+                     void *out, uint64_t stride, uint64_t capacity, uint8_t *found, void *stream) {
+  if (n == 0 || !clients) return set_err(KVS_E_INVAL, "get_parallel: clients must not be empty");
+  if (!keys || !key_lens || !found || !out) return set_err(KVS_E_INVAL, "get_parallel: null argument");
+  for (uint32_t i = 0; i < n; ++i) {
+    if (!clients[i]) return set_err(KVS_E_INVAL, "get_parallel: client %u is null", i);
+    if (clients[i]->device != clients[0]->device)
+      return set_err(KVS_E_INVAL, "get_parallel: all Clients must share one client device (client %u differs)", i);
+  }
+  for (uint32_t i = 0; i < n; ++i) {
+    int f = 0;
+    TRY(kvs_get(clients[i], keys[i], key_lens[i], (uint8_t *)out + i * stride, capacity, &f, nullptr, stream));
+    found[i] = (uint8_t)f;
+  }
+  return KVS_OK;
+}
+
+static int single_key_op(kvs_client *c, const void *key, uint32_t key_len, const char *op,
+                         kvs_server **s_out, uint32_t *slot_out, uint32_t *si_out) {
+  TRY(check_client(c));
+  TRY(validate_key(c, key, key_len, op));
+  const uint32_t si = shard_index(c, (const uint8_t *)key, key_len);
+  kvs_server *s = c->shards[si];
+  TRY(quarantine_on_error(c, s->commit_all()));
+  *s_out = s;
+  *si_out = si;
+  *slot_out = s->dir->lookup((const uint8_t *)key, key_len);
+  return KVS_OK;
+}
+
+int kvs_exists(kvs_client *c, const void *key, uint32_t key_len, int *found) {
+  if (!found) return set_err(KVS_E_INVAL, "exists: found is null");
+  *found = 0;
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(check_client(c));
+  TRY(validate_key(c, key, key_len, "exists"));
+  kvs_server *s = c->shards[shard_index(c, (const uint8_t *)key, key_len)];
+  std::lock_guard<std::mutex> sl(s->mu);
+  kvs_server *s2;
+  uint32_t slot, si;
+  TRY(single_key_op(c, key, key_len, "exists", &s2, &slot, &si));
+  *found = slot != kvs::kBucketEmpty;
+  return KVS_OK;
+}
+
+int kvs_delete(kvs_client *c, const void *key, uint32_t key_len, int *removed) {
+  if (!removed) return set_err(KVS_E_INVAL, "delete: removed is null");
+  *removed = 0;
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(check_client(c));
+  TRY(validate_key(c, key, key_len, "remove"));
+  kvs_server *s = c->shards[shard_index(c, (const uint8_t *)key, key_len)];
+  std::lock_guard<std::mutex> sl(s->mu);
+  kvs_server *s2;
+  uint32_t slot, si;
+  TRY(single_key_op(c, key, key_len, "remove", &s2, &slot, &si));
+  if (slot == kvs::kBucketEmpty) return KVS_OK;
+  s->dir->remove(slot);
+  s->release_dropped();
+  *removed = 1;
+  return KVS_OK;
+}
+
+int kvs_move_to_host(kvs_client *c, const void *key, uint32_t key_len) {
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(check_client(c));
+  TRY(validate_key(c, key, key_len, "move"));
+  kvs_server *s = c->shards[shard_index(c, (const uint8_t *)key, key_len)];
+  std::lock_guard<std::mutex> sl(s->mu);
+  kvs_server *s2;
+  uint32_t slot, si;
+  TRY(single_key_op(c, key, key_len, "move", &s2, &slot, &si));
+  if (slot != kvs::kBucketEmpty) s->dir->move_to_host(slot);
+  return KVS_OK;
+}
+
+int kvs_move_to_device(kvs_client *c, const void *key, uint32_t key_len) {
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(check_client(c));
+  TRY(validate_key(c, key, key_len, "move"));
+  const uint32_t si0 = shard_index(c, (const uint8_t *)key, key_len);
+  kvs_server *s = c->shards[si0];
+  std::lock_guard<std::mutex> sl(s->mu);
+  kvs_server *s2;
+  uint32_t slot, si;
+  TRY(single_key_op(c, key, key_len, "move", &s2, &slot, &si));
+  if (slot == kvs::kBucketEmpty) return KVS_OK;
+  uint64_t off = 0;
+  if (!s->dir->move_to_device(slot, &off)) return KVS_OK;
+  const HostBacking &hb = s->dir->backing(slot);
+  const uint64_t t0 = now_ns();
+  TRY(c->stage.begin(4096 + mutation_upper_bound(s), c->stream));
+  PackedMutations pm = pack_mutations(s, c->stage);
+  TRY(c->stage.upload(c->stream, c->stage.used));
+  TRY(chain_wait(c, s));
+  TRY(quarantine_on_error(c, launch_mutations(c, s, pm)));
+  CUDA_TRY(cudaMemcpyAsync(s->slab + off, s->host_ptr(hb), s->dir->entry(slot).total_len, cudaMemcpyHostToDevice,
+                           c->stream));
+  TRY(chain_record(c, si));
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  s->mprof.to_device_count++;
+  s->mprof.to_device_worker_ns += now_ns() - t0;
+  s->mprof.to_device_complete_ns += now_ns() - t0;
+  s->moves_completed.fetch_add(1, std::memory_order_relaxed);
+  return KVS_OK;
+}
+
+int kvs_flush(kvs_client *c) {
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(check_client(c));
+  std::vector<uint8_t> inv(c->shards.size(), 1);
+  ShardLocks locks(involved_servers(c, inv));
+  return quarantine_on_error(c, commit_barrier(c, inv));
+}
+
+// ---------------------------------------------------------------------------- block path
+
+static int check_blocks(const kvs_block_layout *L, uint32_t n, const uint64_t *keys, const int64_t *block_ids,
+                        const char *op) {
+  if (n == 0) return set_err(KVS_E_INVAL, "%s: empty batch", op);
+  if (!keys || !block_ids) return set_err(KVS_E_INVAL, "%s: keys and block_ids must be non-null", op);
+  for (uint32_t i = 0; i < n; ++i)
+    if (block_ids[i] < 0 || (uint64_t)block_ids[i] >= L->n_pool_blocks)
+      return set_err(KVS_E_INVAL, "%s: block id %lld at %u is outside the %llu-block pool", op,
+                     (long long)block_ids[i], i, (unsigned long long)L->n_pool_blocks);
+  return KVS_OK;
+}
+
+int kvs_put_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const uint64_t *keys,
+                   const int64_t *block_ids, int sync_commit, void *stream) {
+  TRY(check_client(c));
+  BlockFormat fmt;
+  TRY(block_format(layout, &fmt));
+  TRY(check_blocks(layout, n, keys, block_ids, "put_blocks"));
+  for (auto *s : c->shards)
+    if (fmt.value_len > s->cfg.max_value_bytes)
+      return set_err(KVS_E_INVAL, "put_blocks: block value of %llu B exceeds max_value_bytes %llu",
+                     (unsigned long long)fmt.value_len, (unsigned long long)s->cfg.max_value_bytes);
+  const uint64_t t0 = now_ns();
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(validate_layout_ptrs(c, layout, "put_blocks"));
+  std::vector<uint8_t> inv(c->shards.size(), 0);
+  std::vector<uint32_t> si(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    si[i] = shard_index(c, (const uint8_t *)&keys[i], 8);
+    inv[si[i]] = 1;
+  }
+  ShardLocks locks(involved_servers(c, inv));
+  TRY(begin_op(c, stream));
+  PutBatch b{c, layout, &fmt, {}, std::vector<uint8_t>(c->shards.size(), 0)};
+  b.items.reserve(n);
+  const uint64_t t1 = now_ns();
+  for (uint32_t i = 0; i < n; ++i)
+    TRY(quarantine_on_error(c, stage_put(b, si[i], (const uint8_t *)&keys[i], 8, fmt.value_len, block_ids[i], 0)));
+  c->prof.prepare_ns += now_ns() - t1;
+  TRY(quarantine_on_error(c, flush_puts(b, c->stream)));
+  const uint64_t t2 = now_ns();
+  if (sync_commit) TRY(quarantine_on_error(c, commit_barrier(c, inv)));
+  c->prof.commit_wait_ns += now_ns() - t2;
+  TRY(end_op(c, stream));
+  c->prof.count += n;
+  c->prof.total_ns += now_ns() - t0;
+  return KVS_OK;
+}
+
+// Keys of a batch ordered by shard (stable), so each shard's device lookup reads one contiguous
+// run. perm[j] is the batch position of the j-th key in shard order.
+struct ShardOrder {
+  std::vector<uint32_t> perm;
+  std::vector<uint32_t> run_begin, run_shard;  // runs of one shard in `perm` order
+};
+
+static ShardOrder order_by_shard(const std::vector<uint32_t> &si, size_t n_shards) {
+  ShardOrder o;
+  const uint32_t n = (uint32_t)si.size();
+  o.perm.resize(n);
+  if (n_shards == 1) {
+    for (uint32_t i = 0; i < n; ++i) o.perm[i] = i;
+    o.run_begin = {0, n};
+    o.run_shard = {0};
+    return o;
+  }
+  std::vector<uint32_t> count(n_shards + 1, 0);
+  for (uint32_t x : si) count[x + 1]++;
+  for (size_t k = 0; k < n_shards; ++k) count[k + 1] += count[k];
+  std::vector<uint32_t> pos(count.begin(), count.end() - 1);
+  for (uint32_t i = 0; i < n; ++i) o.perm[pos[si[i]]++] = i;
+  for (size_t k = 0; k < n_shards; ++k)
+    if (count[k + 1] > count[k]) {
+      o.run_begin.push_back(count[k]);
+      o.run_shard.push_back((uint32_t)k);
+    }
+  o.run_begin.push_back(n);
+  return o;
+}
+
+// Launch the device index probe for every shard run. keys/out/blob arrays are in shard order.
+static int launch_lookups(kvs_client *c, const ShardOrder &o, const uint8_t *d_keys, kvs::LookupOut *d_out,
+                          uint64_t *d_blob, uint64_t expected_len) {
+  for (size_t r = 0; r + 1 < o.run_begin.size(); ++r) {
+    const uint32_t b0 = o.run_begin[r], b1 = o.run_begin[r + 1];
+    kvs_server *s = c->shards[o.run_shard[r]];
+    kvs::LookupParams lp{};
+    lp.keys = d_keys + 8ull * b0;
+    lp.key_lens = nullptr;
+    lp.key_stride = 8;
+    lp.n = b1 - b0;
+    lp.buckets = s->d_buckets;
+    lp.bucket_mask = s->dir->num_buckets() - 1;
+    lp.meta = s->d_meta;
+    lp.key_rows = s->d_keyrows;
+    lp.max_keys = s->cfg.max_keys;
+    lp.slab_base = s->slab_base();
+    lp.expected_len = expected_len;
+    lp.out = d_out + b0;
+    lp.blob_ptrs = d_blob ? d_blob + b0 : nullptr;
+    CUDA_TRY(kvs::launch_index_lookup(lp, c->stream));
+    s->launches++;
+  }
+  return KVS_OK;
+}
+
+int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const uint64_t *keys,
+                   const int64_t *block_ids, uint8_t *found, void *stream) {
+  TRY(check_client(c));
+  if (!found) return set_err(KVS_E_INVAL, "get_blocks: found is null");
+  BlockFormat fmt;
+  TRY(block_format(layout, &fmt));
+  TRY(check_blocks(layout, n, keys, block_ids, "get_blocks"));
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(validate_layout_ptrs(c, layout, "get_blocks"));
+  const size_t ns = c->shards.size();
+  std::vector<uint8_t> inv(ns, 0);
+  std::vector<uint32_t> si(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    si[i] = shard_index(c, (const uint8_t *)&keys[i], 8);
+    inv[si[i]] = 1;
+  }
+  const ShardOrder ord = order_by_shard(si, ns);
+  ShardLocks locks(involved_servers(c, inv));
+  TRY(quarantine_on_error(c, commit_barrier(c, inv)));  // GET preserves host-commit ordering first
+  TRY(begin_op(c, stream));
+  // ---- pass 1: replica update, device lookup, scatter of device hits
+  Staging &st = c->stage;
+  size_t need = 4096 + 64ull * n + 40ull * layout->n_members;
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) need += mutation_upper_bound(c->shards[i]);
+  TRY(st.begin(need, c->stream));
+  std::vector<PackedMutations> pms(ns);
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) pms[i] = pack_mutations(c->shards[i], st);
+  const size_t keys_off = st.take(8ull * n);
+  const size_t ids_off = st.take(8ull * n);
+  for (uint32_t j = 0; j < n; ++j) {
+    st.h<uint64_t>(keys_off)[j] = keys[ord.perm[j]];
+    st.h<int64_t>(ids_off)[j] = block_ids[ord.perm[j]];
+  }
+  const size_t mp_off = st.push(layout->member_ptrs, 8ull * layout->n_members);
+  const size_t mb_off = st.push(layout->member_block_bytes, 8ull * layout->n_members);
+  const size_t rb_off = st.push(fmt.region_bases.data(), 8ull * layout->n_members);
+  const size_t tp_off = st.push(fmt.tile_prefix.data(), 8ull * (layout->n_members + 1));
+  const size_t upload_bytes = st.used;
+  const size_t out_off = st.take(sizeof(kvs::LookupOut) * n);
+  const size_t blob_off = st.take(8ull * n);
+  TRY(st.upload(c->stream, upload_bytes));
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) TRY(chain_wait(c, c->shards[i]));
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms[i])));
+  TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.d<kvs::LookupOut>(out_off),
+                                            st.d<uint64_t>(blob_off), fmt.value_len)));
+  kvs::ChunkCopyParams p{};
+  p.member_ptrs = st.d<uint64_t>(mp_off);
+  p.member_bytes = st.d<uint64_t>(mb_off);
+  p.region_bases = st.d<uint64_t>(rb_off);
+  p.tile_prefix = st.d<uint64_t>(tp_off);
+  p.block_ids = st.d<int64_t>(ids_off);
+  p.blob_ptrs = st.d<uint64_t>(blob_off);
+  p.n_blobs = n;
+  p.blocks_per_blob = 1;
+  p.n_ranks = 1;
+  p.n_members = layout->n_members;
+  p.tile_bytes = kTileBytes;
+  p.tiles_per_combo = fmt.tile_prefix.back();
+  p.total_tiles = (uint64_t)n * p.tiles_per_combo;
+  p.to_blob = 0;
+  uint64_t payload_per_block = 0;
+  for (uint32_t m = 0; m < layout->n_members; ++m) payload_per_block += layout->member_block_bytes[m];
+  cudaEvent_t t0 = nullptr;
+  c->time_begin(&t0);
+  CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+  c->time_end(t0, 1, (uint64_t)n * payload_per_block);  // misses copy nothing; corrected below
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) c->shards[i]->launches++;
+  CUDA_TRY(cudaMemcpyAsync(st.h<kvs::LookupOut>(out_off), st.d<kvs::LookupOut>(out_off), sizeof(kvs::LookupOut) * n,
+                           cudaMemcpyDeviceToHost, c->stream));
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) TRY(chain_record(c, i));
+  // while the GPU works: the authoritative host lookups
+  std::vector<uint32_t> host_slot(n);
+  for (uint32_t i = 0; i < n; ++i) host_slot[i] = c->shards[si[i]]->dir->lookup((const uint8_t *)&keys[i], 8);
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  std::vector<kvs::LookupOut> res(n);
+  for (uint32_t j = 0; j < n; ++j) res[ord.perm[j]] = st.h<kvs::LookupOut>(out_off)[j];
+  int format_error = -1;
+  for (uint32_t i = 0; i < n; ++i) {
+    const bool dev_hit = res[i].status != kvs::kMiss;
+    const bool host_hit = host_slot[i] != kvs::kBucketEmpty;
+    if (dev_hit != host_hit || (dev_hit && res[i].slot != host_slot[i])) {
+      c->quarantined = true;
+      return set_err(KVS_E_CUDA, "get_blocks: device index replica disagrees with the catalog for key %u", i);
+    }
+    if (res[i].status == kvs::kLenMismatch && format_error < 0) format_error = (int)i;
+  }
+  if (c->timing && !c->timed.empty() && c->timed.back().kind == 1) {
+    uint64_t hits = 0;
+    for (uint32_t i = 0; i < n; ++i) hits += res[i].status == kvs::kHitDevice;
+    c->timed.back().bytes = hits * payload_per_block;
+  }
+  // ---- host processing in batch order: recency, read-through admission
+  struct Late {
+    uint32_t i, shard, slot;
+    uint64_t admit_dst;  // slab address filled from the host copy (0: none)
+    const uint8_t *host;
+    uint64_t len;
+    bool scatter;  // pass 1 did not deliver it (host-tier hit)
+  };
+  std::vector<Late> late;
+  std::map<std::pair<uint32_t, uint32_t>, size_t> admitted;  // (shard, slot) -> index in late
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) c->shards[i]->dir->take_evicted();
+  for (uint32_t i = 0; i < n; ++i) {
+    found[i] = 0;
+    if (res[i].status == kvs::kMiss || res[i].status == kvs::kLenMismatch) continue;
+    kvs_server *s = c->shards[si[i]];
+    uint64_t off = 0;
+    const auto action = s->dir->get_hit(host_slot[i], &off);
+    found[i] = 1;
+    // an admission earlier in this batch whose block was just evicted again: serve that one
+    // from its host copy instead of the (reused) block
+    for (uint32_t ev : s->dir->take_evicted()) {
+      auto it = admitted.find({si[i], ev});
+      if (it != admitted.end()) late[it->second].admit_dst = 0;
+    }
+    if (action == Directory::GetAction::kDevice) continue;
+    const HostBacking &hb = s->dir->backing(host_slot[i]);
+    Late L{i, si[i], host_slot[i], 0, s->host_ptr(hb), s->dir->entry(host_slot[i]).total_len,
+           res[i].status == kvs::kHitHost};
+    if (action == Directory::GetAction::kAdmit) {
+      L.admit_dst = s->slab_base() + off;
+      admitted[{si[i], host_slot[i]}] = late.size();
+    }
+    late.push_back(L);
+  }
+  if (!late.empty()) {
+    // ---- pass 2: replica update, admissions (host -> slab), scatter of host-tier hits
+    size_t need2 = 4096 + 32ull * late.size() + 40ull * layout->n_members;
+    for (size_t i = 0; i < ns; ++i)
+      if (inv[i]) need2 += mutation_upper_bound(c->shards[i]);
+    TRY(st.begin(need2, c->stream));
+    std::vector<PackedMutations> pms2(ns);
+    for (size_t i = 0; i < ns; ++i)
+      if (inv[i]) pms2[i] = pack_mutations(c->shards[i], st);
+    size_t nscatter = 0;
+    for (auto &L : late) nscatter += L.scatter;
+    const size_t blobs2 = st.take(8 * std::max<size_t>(nscatter, 1));
+    const size_t ids2 = st.take(8 * std::max<size_t>(nscatter, 1));
+    size_t k = 0;
+    for (auto &L : late)
+      if (L.scatter) {
+        // admitted values are scattered from their new slab block, others from host memory
+        st.h<uint64_t>(blobs2)[k] = L.admit_dst ? L.admit_dst : reinterpret_cast<uint64_t>(L.host);
+        st.h<int64_t>(ids2)[k] = block_ids[L.i];
+        ++k;
+      }
+    const size_t mp2 = st.push(layout->member_ptrs, 8ull * layout->n_members);
+    const size_t mb2 = st.push(layout->member_block_bytes, 8ull * layout->n_members);
+    const size_t rb2 = st.push(fmt.region_bases.data(), 8ull * layout->n_members);
+    const size_t tp2 = st.push(fmt.tile_prefix.data(), 8ull * (layout->n_members + 1));
+    TRY(st.upload(c->stream, st.used));
+    for (size_t i = 0; i < ns; ++i)
+      if (inv[i]) TRY(chain_wait(c, c->shards[i]));
+    for (size_t i = 0; i < ns; ++i)
+      if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms2[i])));
+    for (auto &L : late)
+      if (L.admit_dst)
+        CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<void *>(L.admit_dst), L.host, L.len, cudaMemcpyHostToDevice,
+                                 c->stream));
+    if (nscatter) {
+      kvs::ChunkCopyParams q = p;
+      q.member_ptrs = st.d<uint64_t>(mp2);
+      q.member_bytes = st.d<uint64_t>(mb2);
+      q.region_bases = st.d<uint64_t>(rb2);
+      q.tile_prefix = st.d<uint64_t>(tp2);
+      q.block_ids = st.d<int64_t>(ids2);
+      q.blob_ptrs = st.d<uint64_t>(blobs2);
+      q.n_blobs = (uint32_t)nscatter;
+      q.total_tiles = (uint64_t)nscatter * q.tiles_per_combo;
+      CUDA_TRY(kvs::launch_chunk_copy(q, c->stream));
+    }
+    for (size_t i = 0; i < ns; ++i)
+      if (inv[i]) TRY(chain_record(c, i));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    for (auto &L : late) {
+      kvs_server *s = c->shards[L.shard];
+      s->mprof.to_device_count++;
+      s->moves_completed.fetch_add(1, std::memory_order_relaxed);
+    }
+  }
+  TRY(end_op(c, stream));
+  if (format_error >= 0)
+    return set_err(KVS_E_FORMAT, "get_blocks: stored value for key %d has length %u, the block layout needs %llu",
+                   format_error, res[format_error].value_len, (unsigned long long)fmt.value_len);
+  return KVS_OK;
+}
+
+int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found) {
+  TRY(check_client(c));
+  if (n == 0) return KVS_OK;
+  if (!keys || !found) return set_err(KVS_E_INVAL, "exists_batch: null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  const size_t ns = c->shards.size();
+  std::vector<uint8_t> inv(ns, 0);
+  std::vector<uint32_t> si(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    si[i] = shard_index(c, (const uint8_t *)&keys[i], 8);
+    inv[si[i]] = 1;
+  }
+  const ShardOrder ord = order_by_shard(si, ns);
+  ShardLocks locks(involved_servers(c, inv));
+  TRY(quarantine_on_error(c, commit_barrier(c, inv)));  // EXISTS fuses the commit wait
+  Staging &st = c->stage;
+  size_t need = 4096 + 48ull * n;
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) need += mutation_upper_bound(c->shards[i]);
+  TRY(st.begin(need, c->stream));
+  std::vector<PackedMutations> pms(ns);
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) pms[i] = pack_mutations(c->shards[i], st);
+  const size_t keys_off = st.take(8ull * n);
+  for (uint32_t j = 0; j < n; ++j) st.h<uint64_t>(keys_off)[j] = keys[ord.perm[j]];
+  const size_t upload_bytes = st.used;
+  const size_t out_off = st.take(sizeof(kvs::LookupOut) * n);
+  TRY(st.upload(c->stream, upload_bytes));
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) TRY(chain_wait(c, c->shards[i]));
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms[i])));
+  TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.d<kvs::LookupOut>(out_off), nullptr, 0)));
+  CUDA_TRY(cudaMemcpyAsync(st.h<kvs::LookupOut>(out_off), st.d<kvs::LookupOut>(out_off), sizeof(kvs::LookupOut) * n,
+                           cudaMemcpyDeviceToHost, c->stream));
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) TRY(chain_record(c, i));
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  for (uint32_t j = 0; j < n; ++j) {
+    const uint32_t i = ord.perm[j];
+    found[i] = st.h<kvs::LookupOut>(out_off)[j].status != kvs::kMiss;
+    const bool host_hit = c->shards[si[i]]->dir->lookup((const uint8_t *)&keys[i], 8) != kvs::kBucketEmpty;
+    if ((bool)found[i] != host_hit) {
+      c->quarantined = true;
+      return set_err(KVS_E_CUDA, "exists_batch: device index replica disagrees with the catalog for key %u", i);
+    }
+  }
+  return KVS_OK;
+}
+
+int kvs_client_set_timing(kvs_client *c, int enable) {
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  c->drain_timing();
+  c->timing = enable != 0;
+  return KVS_OK;
+}
+
+int kvs_client_timing(kvs_client *c, kvs_kernel_timing *gather, kvs_kernel_timing *scatter) {
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  c->drain_timing();
+  if (gather) *gather = c->acc[0];
+  if (scatter) *scatter = c->acc[1];
+  c->acc[0] = kvs_kernel_timing{};
+  c->acc[1] = kvs_kernel_timing{};
+  return KVS_OK;
+}
+
+// ---------------------------------------------------------------------------- chunk ops
+
+static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_members,
+                    const uint64_t *member_block_bytes, const uint64_t *member_extent, const uint32_t *block_ids,
+                    uint32_t n_blocks, const uint64_t *region_bases, const uint32_t *header_words,
+                    uint32_t n_header_words, void *blob, uint64_t blob_bytes, void *stream, int to_blob,
+                    const char *op) {
+  if (n_ranks == 0) return set_err(KVS_E_INVAL, "%s: rank_coords must not be empty", op);
+  if (n_members == 0) return set_err(KVS_E_INVAL, "%s: members must not be empty", op);
+  if (n_blocks == 0) return set_err(KVS_E_INVAL, "%s: block_ids must not be empty", op);
+  if (!member_ptrs || !member_block_bytes || !member_extent || !block_ids || !region_bases || !blob)
+    return set_err(KVS_E_INVAL, "%s: null argument", op);
+  const uint32_t header_bytes = 4 * n_header_words;
+  if (header_bytes % 32) return set_err(KVS_E_INVAL, "%s: header must be 32-byte aligned, got %u B", op, header_bytes);
+  if (header_bytes > blob_bytes)
+    return set_err(KVS_E_INVAL, "%s: %u B header exceeds the %llu B blob", op, header_bytes,
+                   (unsigned long long)blob_bytes);
+  uint32_t max_block = 0;
+  for (uint32_t i = 0; i < n_blocks; ++i) max_block = std::max(max_block, block_ids[i]);
+  std::vector<uint64_t> tile_prefix(n_members + 1, 0);
+  for (uint32_t m = 0; m < n_members; ++m) {
+    const uint64_t sbb = member_block_bytes[m];
+    if (sbb == 0 || sbb % 4)
+      return set_err(KVS_E_INVAL, "%s: member %u block bytes %llu must be nonzero and 4-byte aligned", op, m,
+                     (unsigned long long)sbb);
+    if (region_bases[m] % 32) return set_err(KVS_E_INVAL, "%s: region base %llu must be 32-byte aligned", op,
+                                             (unsigned long long)region_bases[m]);
+    if (region_bases[m] < header_bytes)
+      return set_err(KVS_E_INVAL, "%s: member %u's region at %llu B overlaps the %u B header", op, m,
+                     (unsigned long long)region_bases[m], header_bytes);
+    const uint64_t source_end = ((uint64_t)max_block + 1) * sbb;
+    if (source_end > member_extent[m])
+      return set_err(KVS_E_INVAL, "%s: block %u reaches past member %u's %llu B shard", op, max_block, m,
+                     (unsigned long long)member_extent[m]);
+    const uint64_t end = region_bases[m] + (uint64_t)n_blocks * sbb * n_ranks;
+    if (end > blob_bytes)
+      return set_err(KVS_E_INVAL, "%s: member %u's region ends at %llu B, past the %llu B blob", op, m,
+                     (unsigned long long)end, (unsigned long long)blob_bytes);
+    for (uint32_t r = 0; r < n_ranks; ++r)
+      if (!member_ptrs[(uint64_t)r * n_members + m])
+        return set_err(KVS_E_INVAL, "%s: member %u of rank %u is null", op, m, r);
+    tile_prefix[m + 1] = tile_prefix[m] + (sbb + kTileBytes - 1) / kTileBytes;
+  }
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, blob) != cudaSuccess || (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)) {
+    cudaGetLastError();
+    return set_err(KVS_E_INVAL, "%s: blob must be device memory", op);
+  }
+  DeviceGuard g(a.device);
+  // members on other GPUs are read / written over NVLink: enable peer access to their devices
+  for (uint64_t i = 0; i < (uint64_t)n_ranks * n_members; ++i) {
+    cudaPointerAttributes ma{};
+    if (cudaPointerGetAttributes(&ma, reinterpret_cast<const void *>(member_ptrs[i])) != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(KVS_E_INVAL, "%s: member tensor must be device memory", op);
+    }
+    if (ma.type == cudaMemoryTypeDevice && ma.device != a.device) {
+      cudaError_t pe = cudaDeviceEnablePeerAccess(ma.device, 0);
+      if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else if (pe != cudaSuccess) return set_err(KVS_E_CUDA, "%s: enable peer access %d->%d: %s", op, a.device,
+                                                 ma.device, cudaGetErrorString(pe));
+    }
+  }
+  // per-call device metadata: allocated from a small stream-ordered pool (cudaMallocAsync)
+  const uint64_t nrm = (uint64_t)n_ranks * n_members;
+  const size_t bytes = 8 * (nrm + 3ull * n_members + 1 + n_blocks + 1) + 4ull * n_header_words + 64;
+  std::vector<uint8_t> hostbuf(bytes, 0);
+  size_t off = 0;
+  auto put = [&](const void *src, size_t n) {
+    off = (off + 15) & ~size_t(15);
+    const size_t o = off;
+    if (n) std::memcpy(hostbuf.data() + o, src, n);
+    off += n;
+    return o;
+  };
+  hostbuf.resize(bytes + 16 * 8);
+  std::vector<int64_t> ids64(block_ids, block_ids + n_blocks);
+  const uint64_t blob_addr = reinterpret_cast<uint64_t>(blob);
+  const size_t o_mp = put(member_ptrs, 8 * nrm);
+  const size_t o_mb = put(member_block_bytes, 8ull * n_members);
+  const size_t o_rb = put(region_bases, 8ull * n_members);
+  const size_t o_tp = put(tile_prefix.data(), 8ull * (n_members + 1));
+  const size_t o_id = put(ids64.data(), 8ull * n_blocks);
+  const size_t o_bl = put(&blob_addr, 8);
+  const size_t o_hw = put(header_words, 4ull * n_header_words);
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t *dbuf = nullptr;
+  CUDA_TRY(cudaMallocAsync(&dbuf, off, s));
+  CUDA_TRY(cudaMemcpyAsync(dbuf, hostbuf.data(), off, cudaMemcpyHostToDevice, s));
+  kvs::ChunkCopyParams p{};
+  p.member_ptrs = reinterpret_cast<const uint64_t *>(dbuf + o_mp);
+  p.member_bytes = reinterpret_cast<const uint64_t *>(dbuf + o_mb);
+  p.region_bases = reinterpret_cast<const uint64_t *>(dbuf + o_rb);
+  p.tile_prefix = reinterpret_cast<const uint64_t *>(dbuf + o_tp);
+  p.block_ids = reinterpret_cast<const int64_t *>(dbuf + o_id);
+  p.blob_ptrs = reinterpret_cast<const uint64_t *>(dbuf + o_bl);
+  p.header_words = reinterpret_cast<const uint32_t *>(dbuf + o_hw);
+  p.n_header_words = to_blob ? n_header_words : 0;
+  p.n_blobs = 1;
+  p.blocks_per_blob = n_blocks;
+  p.n_ranks = n_ranks;
+  p.n_members = n_members;
+  p.tile_bytes = kTileBytes;
+  p.tiles_per_combo = tile_prefix[n_members];
+  p.total_tiles = (uint64_t)n_blocks * n_ranks * p.tiles_per_combo;
+  p.to_blob = to_blob;
+  CUDA_TRY(kvs::launch_chunk_copy(p, s));
+  CUDA_TRY(cudaFreeAsync(dbuf, s));
+  // the host buffer was consumed by a pageable copy, which completes before returning
+  return KVS_OK;
+}
+
+int kvs_gather_chunk(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_members,
+                     const uint64_t *member_block_bytes, const uint64_t *member_extent, const uint32_t *block_ids,
+                     uint32_t n_blocks, const uint64_t *region_bases, const uint32_t *header_words,
+                     uint32_t n_header_words, void *blob, uint64_t blob_bytes, void *stream) {
+  return chunk_op(member_ptrs, n_ranks, n_members, member_block_bytes, member_extent, block_ids, n_blocks,
+                  region_bases, header_words, n_header_words, blob, blob_bytes, stream, 1, "kvcache gather");
+}
+
+int kvs_scatter_chunk(const void *blob, uint64_t blob_bytes, const uint64_t *member_ptrs, uint32_t n_ranks,
+                      uint32_t n_members, const uint64_t *member_block_bytes, const uint64_t *member_extent,
+                      const uint32_t *block_ids, uint32_t n_blocks, const uint64_t *region_bases, void *stream) {
+  return chunk_op(member_ptrs, n_ranks, n_members, member_block_bytes, member_extent, block_ids, n_blocks,
+                  region_bases, nullptr, 0, const_cast<void *>(blob), blob_bytes, stream, 0, "kvcache scatter");
+}
+
+}  // extern "C"
