@@ -1291,12 +1291,12 @@ int kvo_get_blocks(kvo_store *s, uint8_t *const *members, uint32_t n_members, ui
                 (unsigned long long)s->dir[slot].total_len);
       break;
     }
-    uint64_t before = s->n_copies;
     int fnd = 0;
     rc = get_one(s, kb, 8, NULL, f.value_len, &fnd, NULL, 1);
     if (rc) break;
-    /* replace the copy into NULL by per-member block copies from the same source */
-    for (uint64_t c = before; c < s->n_copies; ++c) {
+    /* replace the copy into NULL by per-member block copies from the same source; get_one may
+     * have flushed the list before an admission, so search all of it */
+    for (uint64_t c = 0; c < s->n_copies; ++c) {
       if (s->copies[c].dst != NULL) continue;
       const uint8_t *src = s->copies[c].src;
       s->copies[c] = s->copies[--s->n_copies];

@@ -90,7 +90,8 @@ def test_random_chunks_match_oracle(ops, seed, n_ranks, n_members, sbb, n_blocks
     block_ids = [int(b) for b in rng.permutation(pool)[:n_blocks]]
     words = O.header_words(n_members, [n_blocks * sbb * n_ranks] * n_members).tolist()
     hdr = 4 * len(words)
-    rb = [hdr + m * (n_blocks * sbb * n_ranks + 32) for m in range(n_members)]  # gaps between regions
+    region = (n_blocks * sbb * n_ranks + 32 + 31) // 32 * 32  # 32-aligned regions with gaps between
+    rb = [hdr + m * region for m in range(n_members)]
     blob_bytes = rb[-1] + n_blocks * sbb * n_ranks + 64
     ref = O.gather(host, [sbb] * n_members, block_ids, rb, words, blob_bytes)
     dev = [[torch.from_numpy(a).cuda() for a in r] for r in host]

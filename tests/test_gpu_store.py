@@ -136,10 +136,11 @@ def test_config1_block_roundtrip(store):
     got = c.get_blocks(layout, keys, dst)
     assert got.all()
     members = [t for pair in kv for t in pair]
+    untouched = torch.as_tensor(np.setdiff1d(np.arange(1024), dst), device="cuda")
     for m, t in enumerate(members):
-        assert torch.equal(t[torch.as_tensor(dst, device="cuda")], snapshot[m][torch.as_tensor(src, device="cuda")])
-        untouched = np.setdiff1d(np.arange(1024), dst)
-        assert torch.equal(t[torch.as_tensor(untouched, device="cuda")], snapshot[m][torch.as_tensor(untouched, device="cuda")])
+        bits, ref = t.view(torch.int16), snapshot[m].view(torch.int16)  # bitwise, not float compare
+        assert torch.equal(bits[torch.as_tensor(dst, device="cuda")], ref[torch.as_tensor(src, device="cuda")])
+        assert torch.equal(bits[untouched], ref[untouched])
     # the stored value is the reference blob of one block: check against the oracle's gather
     seg = 8 * 32 * 128 * 2
     words, rb, vlen = O.chunk_plan(2, seg)
@@ -180,7 +181,8 @@ def test_fp8_with_per_block_scales_roundtrip(store):
     snap = [t.clone() for t in members]
     assert c.get_blocks(layout, keys, dst).all()
     for a, b in zip(members, snap):
-        assert torch.equal(a.view(torch.uint8)[torch.as_tensor(dst).cuda()], b.view(torch.uint8)[torch.as_tensor(src).cuda()])
+        ab, bb = a.view(torch.uint8).reshape(nb, -1), b.view(torch.uint8).reshape(nb, -1)
+        assert torch.equal(ab[torch.as_tensor(dst).cuda()], bb[torch.as_tensor(src).cuda()])
     # value format against the oracle
     mb = layout.member_block_bytes
     words, rb, vlen = O.block_format(mb, 3)

@@ -154,3 +154,33 @@ def test_block_put_get_roundtrip_multithreaded():
     for m in range(4):
         for i in range(16):
             assert np.array_equal(out[m][dst[i] * seg:(dst[i] + 1) * seg], members[m][src[i] * seg:(src[i] + 1) * seg])
+
+
+def test_block_path_under_eviction_serves_host_tier_bytes():
+    """get_blocks with host-tier hits and read-through admissions that evict in the same batch."""
+    seg, pool = 2 * 16 * 64 * 2, 96
+    mb = [seg] * 4
+    _, _, vlen = O.block_format(mb)
+    units = -(-vlen // U)
+    heap = 12 * (1 << (units - 1).bit_length()) * U
+    s = O.Store(max_keys=128, heap_bytes=heap, host_pool_bytes=64 << 20)
+    rng = np.random.default_rng(7)
+    host = [rng.integers(0, 256, pool * seg, dtype=np.uint8) for _ in range(4)]
+    keys = rng.integers(1, 2**63, 48, dtype=np.uint64)
+    truth = {}
+    for r in range(6):
+        idx = rng.choice(48, 8, replace=False)
+        src = rng.choice(48, 8, replace=False)
+        s.put_blocks(host, mb, keys[idx], src)
+        for k, b in zip(idx, src):
+            truth[int(k)] = [h[b * seg:(b + 1) * seg].copy() for h in host]
+        g = rng.choice(48, 12, replace=False)
+        dst = 48 + rng.choice(48, 12, replace=False)
+        found = s.get_blocks(host, mb, keys[g], dst, n_threads=3)
+        for k, d, f in zip(g, dst, found):
+            assert f == (int(k) in truth)
+            if f:
+                for m in range(4):
+                    assert np.array_equal(host[m][d * seg:(d + 1) * seg], truth[int(k)][m])
+    st = s.stats()
+    assert st["admissions"] > 0 and st["victims_evicted"] > 0

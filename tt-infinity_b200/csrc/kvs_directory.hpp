@@ -143,6 +143,7 @@ class Directory {
   const uint32_t *bucket_pairs() const { return buckets_.data(); }
 
   uint32_t lru_order(uint32_t *out, uint32_t cap) const;
+  uint32_t lru_size() const { return lru_count_; }
   uint64_t live_device_bytes() const { return live_bytes_; }
   uint64_t pending_device_bytes() const { return pending_bytes_; }
   uint32_t epoch() const { return epoch_; }

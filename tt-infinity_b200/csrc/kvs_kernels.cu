@@ -214,9 +214,21 @@ int sm_count() {
 
 }  // namespace
 
+// Resident CTAs per SM of the copy kernel (its register use decides it), so a grid-stride
+// launch never has CTAs waiting for a second wave.
+int copy_ctas_per_sm() {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chunk_copy_kernel, kCopyThreads, 0) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 1;
+  }
+  return per_sm;
+}
+
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas) {
   if (p.total_tiles == 0 && (p.n_header_words == 0 || !p.to_blob)) return cudaSuccess;
-  uint64_t grid = grid_ctas > 0 ? (uint64_t)grid_ctas : (uint64_t)sm_count() * (2048 / kCopyThreads);
+  uint64_t grid = grid_ctas > 0 ? (uint64_t)grid_ctas : (uint64_t)sm_count() * copy_ctas_per_sm();
   if (grid > p.total_tiles && p.total_tiles > 0) grid = p.total_tiles;
   if (grid == 0) grid = 1;
   chunk_copy_kernel<<<(unsigned)grid, kCopyThreads, 0, stream>>>(p);

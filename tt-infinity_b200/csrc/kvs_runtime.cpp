@@ -1044,7 +1044,11 @@ int kvs_server_index_snapshot(kvs_server *s, uint32_t *host_pairs, uint32_t *dev
 int kvs_server_lru_order(kvs_server *s, uint32_t *slots, uint32_t cap, uint32_t *n) {
   if (!s || !n) return set_err(KVS_E_INVAL, "null argument");
   std::lock_guard<std::mutex> lk(s->mu);
-  *n = s->dir->lru_order(slots, slots ? cap : 0);
+  if (!slots) {  // size query
+    *n = s->dir->lru_size();
+    return KVS_OK;
+  }
+  *n = s->dir->lru_order(slots, cap);
   return KVS_OK;
 }
 
