@@ -58,7 +58,15 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-samples", type=int, default=40)
-    return ap.parse_args()
+    ap.add_argument("--small", action="store_true",
+                    help="profiling case: 16 layers, 512-block pool, 64 blocks per step (same kernels)")
+    args = ap.parse_args()
+    if args.small:
+        global LAYERS, POOL_BLOCKS, BATCH_BLOCKS, BLOCK_PAYLOAD, WORKLOAD
+        LAYERS, POOL_BLOCKS, BATCH_BLOCKS = 16, 512, 64
+        BLOCK_PAYLOAD = 2 * LAYERS * SEG_BYTES
+        WORKLOAD = "qwen3-32b-shaped-16-layer-profiling-case"
+    return args
 
 
 def dist_env():
@@ -87,6 +95,9 @@ class ClockSampler:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
                  "-i", ",".join(str(g) for g in self.gpus)], stdout=self.f, stderr=subprocess.DEVNULL)
+            t0 = time.time()  # the timed region starts once the first sample is in
+            while time.time() - t0 < 5 and self.path.stat().st_size == 0:
+                time.sleep(0.05)
         except Exception:
             self.proc = None
 
@@ -268,6 +279,19 @@ def run_ours(args, rank, local_rank, world):
     p50 = lat[len(lat) // 2]
     p99 = lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)]
 
+    # ---- PCIe device->host copy peak (pinned), the bound of the host write-through
+    pin = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    src_buf = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    best = 0.0
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        pin.copy_(src_buf, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        best = max(best, (1 << 30) / (e0.elapsed_time(e1) / 1e3) / GB)
+    del pin, src_buf
+
     # ---- roofline of the dominant kernel (gather or scatter, by device time)
     peak, peak_kind = measured_peaks()
     g, s = timing["gather"], timing["scatter"]
@@ -302,8 +326,8 @@ def run_ours(args, rank, local_rank, world):
             "workload": WORKLOAD,
             "layers": LAYERS, "kv_heads": HEADS, "head_dim": HEAD_DIM, "block_tokens": BLOCK_TOKENS,
             "pool_blocks": POOL_BLOCKS, "blocks_per_step": BATCH_BLOCKS, "bytes_per_block": BLOCK_PAYLOAD,
-            "step": "put 128 blocks (gather + host write-through) then get 128 blocks (100% device hit)",
-            "l2": "inputs larger than L2 (2 GiB moved per direction per step)",
+            "step": f"put {BATCH_BLOCKS} blocks (gather + host write-through) then get {BATCH_BLOCKS} blocks (100% device hit)",
+            "l2": f"inputs larger than L2 ({BATCH_BLOCKS * BLOCK_PAYLOAD / 2**30:.2f} GiB moved per direction per step)",
             "parallelism": f"dp{world} (independent shard per GPU)",
             "slab_bytes": slab_values * block_units * UNIT_BYTES,
         },
@@ -326,6 +350,13 @@ def run_ours(args, rank, local_rank, world):
                            "GBps_2x_payload": round(2 * g["bytes"] / max(1e-9, g["total_ms"] / 1e3) / GB, 1)},
             "scatter_get": {"launches": s["launches"], "avg_ms": round(s["total_ms"] / max(1, s["launches"]), 4),
                             "GBps_2x_payload": round(2 * s["bytes"] / max(1e-9, s["total_ms"] / 1e3) / GB, 1)},
+        },
+        "write_through": {
+            "bytes_per_step": BATCH_BLOCKS * BLOCK_PAYLOAD,
+            "achieved_GBps": round(BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB, 2),
+            "pcie_d2h_peak_GBps": round(best, 2),
+            "frac": round(BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB / best, 4),
+            "note": "every put is written through to the pinned host tier and get waits for it (commit barrier)",
         },
         "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
                                      "samples": len(lat)},
