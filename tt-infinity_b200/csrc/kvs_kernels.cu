@@ -102,6 +102,185 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const ChunkCop
   }
 }
 
+// ---------------------------------------------------------------- TMA bulk-copy engine
+//
+// One elected thread per CTA streams the CTA's tiles through a ring of kStages shared-memory
+// stages: cp.async.bulk global->shared (completion counted on a per-stage mbarrier), then
+// cp.async.bulk shared->global (one bulk group per tile). Up to kStages-1 loads are in flight per
+// CTA, independent of register pressure. A stage is refilled only after the bulk store that last
+// read it has finished reading (wait_group.read). No multicast: every load reads this CTA's own
+// tile. Tiles that are not 16-byte aligned in address and length (e.g. 4-byte per-block scales)
+// are copied by the CTA's other warps with ordinary loads and stores.
+
+constexpr int kTmaThreads = 128;
+constexpr int kTmaStages = 6;
+constexpr uint32_t kTmaTile = 32u << 10;
+constexpr size_t kTmaSmem = (size_t)kTmaStages * kTmaTile;
+constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier waits (seconds at most), then give up
+
+__device__ unsigned int g_tma_timeouts = 0;  // read by the host after a synchronising call
+
+struct TileRef {
+  uint8_t *member;
+  uint8_t *blob;
+  uint64_t len;
+  bool skip;
+};
+
+__device__ __forceinline__ TileRef tile_ref(const ChunkCopyParams &p, uint64_t t) {
+  TileRef r{};
+  const uint64_t tpc = p.tiles_per_combo;
+  const uint64_t combo = t / tpc;
+  const uint64_t rem = t - combo * tpc;
+  uint32_t lo = 0, hi = p.n_members;
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (p.tile_prefix[mid] <= rem) lo = mid; else hi = mid;
+  }
+  const uint32_t m = lo;
+  const uint64_t tile_in_seg = rem - p.tile_prefix[m];
+  const uint32_t rk = (uint32_t)(combo % p.n_ranks);
+  const uint64_t bc = combo / p.n_ranks;
+  const uint32_t cb = (uint32_t)(bc % p.blocks_per_blob);
+  const uint32_t blob = (uint32_t)(bc / p.blocks_per_blob);
+  const uint64_t blob_base = p.blob_ptrs[blob];
+  if (blob_base == 0) {
+    r.skip = true;
+    return r;
+  }
+  const uint64_t sbb = p.member_bytes[m];
+  const uint64_t seg_off = tile_in_seg * p.tile_bytes;
+  r.len = (sbb - seg_off) < p.tile_bytes ? (sbb - seg_off) : p.tile_bytes;
+  const int64_t block = p.block_ids[(uint64_t)blob * p.blocks_per_blob + cb];
+  r.member = reinterpret_cast<uint8_t *>(p.member_ptrs[(uint64_t)rk * p.n_members + m]) + (uint64_t)block * sbb + seg_off;
+  r.blob = reinterpret_cast<uint8_t *>(blob_base) + p.region_bases[m] + (uint64_t)cb * sbb * p.n_ranks +
+           (uint64_t)rk * sbb + seg_off;
+  r.skip = false;
+  return r;
+}
+
+__device__ __forceinline__ bool tma_ok(const TileRef &r) {
+  return ((reinterpret_cast<uint64_t>(r.member) | reinterpret_cast<uint64_t>(r.blob) | r.len) & 15u) == 0;
+}
+
+__device__ __forceinline__ void bulk_wait_read(int allowed) {
+  switch (allowed) {  // the group count is an immediate
+    case 0: asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.bulk.wait_group.read 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); break;
+    default: asm volatile("cp.async.bulk.wait_group.read 4;" ::: "memory"); break;
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t spin = 0; spin < kSpinLimit; ++spin) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const ChunkCopyParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full_bar[kTmaStages];
+  const uint32_t tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kTmaStages; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&full_bar[s])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid >= 32) {
+    // helper warps: header words (gather) and tiles the bulk engine cannot take
+    const uint32_t h = tid - 32, nh = kTmaThreads - 32;
+    if (p.to_blob && p.n_header_words) {
+      const uint64_t total = (uint64_t)p.n_blobs * p.n_header_words;
+      for (uint64_t g = (uint64_t)blockIdx.x * nh + h; g < total; g += (uint64_t)gridDim.x * nh) {
+        const uint32_t b = (uint32_t)(g / p.n_header_words), w = (uint32_t)(g % p.n_header_words);
+        const uint64_t base = p.blob_ptrs[b];
+        if (base) reinterpret_cast<uint32_t *>(base)[w] = p.header_words[w];
+      }
+    }
+    for (uint64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      const TileRef r = tile_ref(p, t);
+      if (r.skip || tma_ok(r)) continue;
+      uint8_t *dst = p.to_blob ? r.blob : r.member;
+      const uint8_t *src = p.to_blob ? r.member : r.blob;
+      if (((reinterpret_cast<uint64_t>(dst) | reinterpret_cast<uint64_t>(src) | r.len) & 3u) == 0) {
+        for (uint64_t i = h; i < (r.len >> 2); i += nh)
+          reinterpret_cast<uint32_t *>(dst)[i] = reinterpret_cast<const uint32_t *>(src)[i];
+      } else {
+        for (uint64_t i = h; i < r.len; i += nh) dst[i] = src[i];
+      }
+    }
+    return;
+  }
+  if (tid != 0) return;
+  const uint32_t smem_base = (uint32_t)__cvta_generic_to_shared(smem);
+  uint64_t k_load = 0, k_done = 0;  // positions in this CTA's list of bulk tiles
+  uint64_t t_load = blockIdx.x, t_done = blockIdx.x;  // tile cursors (skip non-bulk tiles)
+  auto next_bulk = [&](uint64_t t, TileRef *out) -> uint64_t {
+    for (; t < p.total_tiles; t += gridDim.x) {
+      const TileRef r = tile_ref(p, t);
+      if (!r.skip && tma_ok(r)) {
+        *out = r;
+        return t;
+      }
+    }
+    return p.total_tiles;
+  };
+  TileRef rl{}, rd{};
+  t_load = next_bulk(t_load, &rl);
+  t_done = t_load;
+  rd = rl;
+  bool failed = false;
+  while (t_done < p.total_tiles && !failed) {
+    // keep up to kTmaStages - 2 loads ahead of the tile being stored
+    while (t_load < p.total_tiles && k_load - k_done < (uint64_t)(kTmaStages - 2)) {
+      const int stage = (int)(k_load % kTmaStages);
+      if (k_load >= (uint64_t)kTmaStages) {
+        // the store of tile k_load - kTmaStages (group k_load - kTmaStages) must have read the stage
+        const int64_t allowed = (int64_t)k_done - 1 - ((int64_t)k_load - kTmaStages);
+        bulk_wait_read(allowed < 0 ? 0 : (int)allowed);
+      }
+      const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&full_bar[stage]);
+      const uint32_t dst = smem_base + (uint32_t)stage * kTmaTile;
+      const uint8_t *src = p.to_blob ? rl.member : rl.blob;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)rl.len) : "memory");
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+          "l"(src), "r"((uint32_t)rl.len), "r"(bar)
+          : "memory");
+      ++k_load;
+      t_load = next_bulk(t_load + gridDim.x, &rl);
+    }
+    const int stage = (int)(k_done % kTmaStages);
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&full_bar[stage]);
+    if (!mbar_wait(bar, (uint32_t)((k_done / kTmaStages) & 1))) {
+      atomicAdd(&g_tma_timeouts, 1u);
+      failed = true;
+      // give the loads still in flight a bounded chance to land before the CTA exits
+      for (uint64_t j = k_done + 1; j < k_load; ++j)
+        mbar_wait((uint32_t)__cvta_generic_to_shared(&full_bar[j % kTmaStages]), (uint32_t)((j / kTmaStages) & 1));
+      break;
+    }
+    uint8_t *dst = p.to_blob ? rd.blob : rd.member;
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                 "r"(smem_base + (uint32_t)stage * kTmaTile), "r"((uint32_t)rd.len)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    ++k_done;
+    t_done = next_bulk(t_done + gridDim.x, &rd);
+  }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // One warp per key. Lane i holds key word i; lane 0 computes the FNV-1a hash.
 __global__ void index_lookup_kernel(const LookupParams p) {
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -234,6 +413,29 @@ cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int
   chunk_copy_kernel<<<(unsigned)grid, kCopyThreads, 0, stream>>>(p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream) {
+  if (p.total_tiles == 0 && (p.n_header_words == 0 || !p.to_blob)) return cudaSuccess;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(chunk_copy_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kTmaSmem);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  uint64_t grid = (uint64_t)sm_count();
+  if (grid > p.total_tiles && p.total_tiles > 0) grid = p.total_tiles;
+  if (grid == 0) grid = 1;
+  chunk_copy_tma_kernel<<<(unsigned)grid, kTmaThreads, kTmaSmem, stream>>>(p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+cudaError_t read_tma_timeouts(unsigned int *count) {
+  return cudaMemcpyFromSymbol(count, g_tma_timeouts, sizeof(unsigned int));
 }
 
 cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream) {

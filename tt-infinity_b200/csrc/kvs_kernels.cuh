@@ -101,6 +101,10 @@ struct MutationParams {
 // Launch helpers (return cudaError_t of the launch). `grid_ctas` = 0 picks the default
 // persistent grid (SM count x resident CTAs per SM).
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas = 0);
+// TMA bulk-copy variant (sources and destinations in device memory, this GPU's or a peer's).
+cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream);
+// Bounded-wait expiries of the bulk-copy engine on the current device (0 in normal operation).
+cudaError_t read_tma_timeouts(unsigned int *count);
 cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream);
 cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream);
 cudaError_t launch_echo(const uint8_t *in, uint8_t *out, uint32_t n, cudaStream_t stream);

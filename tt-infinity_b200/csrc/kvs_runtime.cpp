@@ -366,6 +366,30 @@ struct kvs_client {
 
 namespace {
 
+// Copy-engine choice: the TMA bulk engine for device memory (this GPU's or a peer's), the
+// LDG/STG engine when a side is host memory. KVS_COPY_ENGINE=ldg forces the LDG engine.
+bool tma_enabled() {
+  static const bool on = [] {
+    const char *v = std::getenv("KVS_COPY_ENGINE");
+    return !(v && std::strcmp(v, "ldg") == 0);
+  }();
+  return on;
+}
+
+cudaError_t launch_copy(const kvs::ChunkCopyParams &p, cudaStream_t stream, bool device_memory_only) {
+  if (device_memory_only && tma_enabled()) return kvs::launch_chunk_copy_tma(p, stream);
+  return kvs::launch_chunk_copy(p, stream);
+}
+
+// Bounded waits in the bulk engine that expired (never in normal operation) turn into an error.
+int check_tma_timeouts(const char *op) {
+  unsigned int n = 0;
+  cudaError_t e = kvs::read_tma_timeouts(&n);
+  if (e != cudaSuccess) return set_err(KVS_E_CUDA, "%s: reading the copy-engine status: %s", op, cudaGetErrorString(e));
+  if (n) return set_err(KVS_E_TIMEOUT, "%s: %u copy-engine waits expired", op, n);
+  return KVS_OK;
+}
+
 int check_client(kvs_client *c) {
   if (!c) return set_err(KVS_E_INVAL, "client handle is null");
   if (c->closed) return set_err(KVS_E_CLOSED, "client is closed");
@@ -395,7 +419,7 @@ int check_device_ptr(kvs_client *c, const void *p, const char *op, const char *w
     cudaGetLastError();
     return set_err(KVS_E_INVAL, "%s: %s must use DEVICE storage", op, what);
   }
-  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+  if (a.type != cudaMemoryTypeDevice)
     return set_err(KVS_E_INVAL, "%s: %s must use DEVICE storage", op, what);
   if (a.type == cudaMemoryTypeDevice && a.device != c->device)
     return set_err(KVS_E_INVAL, "%s: %s must belong to the client device %d; got device %d", op, what,
@@ -666,7 +690,7 @@ int flush_puts(PutBatch &b, cudaStream_t) {
       p.to_blob = 1;
       cudaEvent_t t0 = nullptr;
       c->time_begin(&t0);
-      CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+      CUDA_TRY(launch_copy(p, c->stream, true));
       c->time_end(t0, 0, (uint64_t)n * (b.fmt->value_len - 4ull * b.fmt->header.size()));
     } else {
       for (size_t i = 0; i < n; ++i) {
@@ -686,7 +710,7 @@ int flush_puts(PutBatch &b, cudaStream_t) {
         p.tiles_per_combo = (b.items[i].len + kTileBytes - 1) / kTileBytes;
         p.total_tiles = p.tiles_per_combo;
         p.to_blob = 1;
-        CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+        CUDA_TRY(launch_copy(p, c->stream, true));
       }
     }
     for (size_t i = 0; i < ns; ++i)
@@ -765,7 +789,8 @@ int quarantine_on_error(kvs_client *c, int rc) {
   return rc;
 }
 
-// Copy one value between a slab location and a buffer with the copy engine kernel.
+// Copy one value between a slab location and a buffer with a copy engine. dst != 0 marks both
+// sides as device memory (bulk engine); 0 means the source is host memory (LDG engine).
 int launch_value_copy(kvs_client *c, uint64_t dst, uint64_t src, uint64_t len, size_t rec_off) {
   // rec layout: {member ptr(dst buffer), bytes, region base 0, tile prefix[2], blob ptr(src)}
   uint64_t *r = c->stage.h<uint64_t>(rec_off);
@@ -787,7 +812,7 @@ int launch_value_copy(kvs_client *c, uint64_t dst, uint64_t src, uint64_t len, s
   p.to_blob = 0;
   (void)dst;
   (void)src;
-  CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+  CUDA_TRY(launch_copy(p, c->stream, dst != 0));
   return KVS_OK;
 }
 
@@ -1266,10 +1291,11 @@ int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_
   TRY(quarantine_on_error(c, launch_mutations(c, s, pm)));
   if (action == Directory::GetAction::kAdmit)
     CUDA_TRY(cudaMemcpyAsync(s->slab + admit_off, s->host_ptr(hb), len, cudaMemcpyHostToDevice, c->stream));
-  TRY(quarantine_on_error(c, launch_value_copy(c, 0, 0, len, rec)));
+  TRY(quarantine_on_error(c, launch_value_copy(c, action == Directory::GetAction::kHostOnly ? 0 : 1, 0, len, rec)));
   s->launches++;
   TRY(chain_record(c, si));
   CUDA_TRY(cudaStreamSynchronize(c->stream));
+  TRY(quarantine_on_error(c, check_tma_timeouts("get")));
   if (action != Directory::GetAction::kDevice) {
     s->mprof.to_device_count++;
     s->moves_completed.fetch_add(1, std::memory_order_relaxed);
@@ -1581,7 +1607,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
   for (uint32_t m = 0; m < layout->n_members; ++m) payload_per_block += layout->member_block_bytes[m];
   cudaEvent_t t0 = nullptr;
   c->time_begin(&t0);
-  CUDA_TRY(kvs::launch_chunk_copy(p, c->stream));
+  CUDA_TRY(launch_copy(p, c->stream, true));
   c->time_end(t0, 1, (uint64_t)n * payload_per_block);  // misses copy nothing; corrected below
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) c->shards[i]->launches++;
@@ -1593,6 +1619,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
   std::vector<uint32_t> host_slot(n);
   for (uint32_t i = 0; i < n; ++i) host_slot[i] = c->shards[si[i]]->dir->lookup((const uint8_t *)&keys[i], 8);
   CUDA_TRY(cudaStreamSynchronize(c->stream));
+  TRY(quarantine_on_error(c, check_tma_timeouts("get_blocks")));
   std::vector<kvs::LookupOut> res(n);
   for (uint32_t j = 0; j < n; ++j) res[ord.perm[j]] = st.h<kvs::LookupOut>(out_off)[j];
   int format_error = -1;
@@ -1689,7 +1716,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
       q.blob_ptrs = st.d<uint64_t>(blobs2);
       q.n_blobs = (uint32_t)nscatter;
       q.total_tiles = (uint64_t)nscatter * q.tiles_per_combo;
-      CUDA_TRY(kvs::launch_chunk_copy(q, c->stream));
+      CUDA_TRY(launch_copy(q, c->stream, false));
     }
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) TRY(chain_record(c, i));
@@ -1823,7 +1850,7 @@ static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_me
     tile_prefix[m + 1] = tile_prefix[m] + (sbb + kTileBytes - 1) / kTileBytes;
   }
   cudaPointerAttributes a{};
-  if (cudaPointerGetAttributes(&a, blob) != cudaSuccess || (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)) {
+  if (cudaPointerGetAttributes(&a, blob) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
     cudaGetLastError();
     return set_err(KVS_E_INVAL, "%s: blob must be device memory", op);
   }
@@ -1831,7 +1858,8 @@ static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_me
   // members on other GPUs are read / written over NVLink: enable peer access to their devices
   for (uint64_t i = 0; i < (uint64_t)n_ranks * n_members; ++i) {
     cudaPointerAttributes ma{};
-    if (cudaPointerGetAttributes(&ma, reinterpret_cast<const void *>(member_ptrs[i])) != cudaSuccess) {
+    if (cudaPointerGetAttributes(&ma, reinterpret_cast<const void *>(member_ptrs[i])) != cudaSuccess ||
+        ma.type != cudaMemoryTypeDevice) {
       cudaGetLastError();
       return set_err(KVS_E_INVAL, "%s: member tensor must be device memory", op);
     }
@@ -1885,7 +1913,7 @@ static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_me
   p.tiles_per_combo = tile_prefix[n_members];
   p.total_tiles = (uint64_t)n_blocks * n_ranks * p.tiles_per_combo;
   p.to_blob = to_blob;
-  CUDA_TRY(kvs::launch_chunk_copy(p, s));
+  CUDA_TRY(launch_copy(p, s, true));
   CUDA_TRY(cudaFreeAsync(dbuf, s));
   // the host buffer was consumed by a pageable copy, which completes before returning
   return KVS_OK;
