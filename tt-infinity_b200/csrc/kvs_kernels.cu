@@ -186,10 +186,82 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   return false;
 }
 
+// Walks a contiguous range of tiles in order. Member values are reloaded only when the walk
+// crosses into the next member, blob values only when it crosses into the next blob.
+struct TileCursor {
+  const ChunkCopyParams *p;
+  uint64_t t, end;
+  uint64_t combo;
+  uint32_t m, rk, cb, blob;
+  uint64_t tile_in_seg, tiles_m, sbb, blob_base;
+  int64_t block;
+
+  __device__ void load_member() {
+    tiles_m = p->tile_prefix[m + 1] - p->tile_prefix[m];
+    sbb = p->member_bytes[m];
+  }
+  __device__ void load_combo() {
+    rk = (uint32_t)(combo % p->n_ranks);
+    const uint64_t bc = combo / p->n_ranks;
+    cb = (uint32_t)(bc % p->blocks_per_blob);
+    blob = (uint32_t)(bc / p->blocks_per_blob);
+    blob_base = blob < p->n_blobs ? p->blob_ptrs[blob] : 0;
+    block = blob < p->n_blobs ? p->block_ids[(uint64_t)blob * p->blocks_per_blob + cb] : 0;
+  }
+  __device__ void init(const ChunkCopyParams *pp, uint64_t begin, uint64_t stop) {
+    p = pp;
+    t = begin;
+    end = stop;
+    if (t >= end) return;
+    const uint64_t tpc = p->tiles_per_combo;
+    combo = t / tpc;
+    const uint64_t rem = t - combo * tpc;
+    uint32_t lo = 0, hi = p->n_members;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (p->tile_prefix[mid] <= rem) lo = mid; else hi = mid;
+    }
+    m = lo;
+    tile_in_seg = rem - p->tile_prefix[m];
+    load_member();
+    load_combo();
+  }
+  __device__ void advance() {
+    ++t;
+    if (++tile_in_seg < tiles_m) return;
+    tile_in_seg = 0;
+    if (++m == p->n_members) {
+      m = 0;
+      ++combo;
+      load_combo();
+    }
+    load_member();
+  }
+  __device__ TileRef ref() const {
+    TileRef r{};
+    if (blob_base == 0) {
+      r.skip = true;
+      return r;
+    }
+    const uint64_t seg_off = tile_in_seg * p->tile_bytes;
+    r.len = (sbb - seg_off) < p->tile_bytes ? (sbb - seg_off) : p->tile_bytes;
+    r.member = reinterpret_cast<uint8_t *>(p->member_ptrs[(uint64_t)rk * p->n_members + m]) + (uint64_t)block * sbb +
+               seg_off;
+    r.blob = reinterpret_cast<uint8_t *>(blob_base) + p->region_bases[m] + (uint64_t)cb * sbb * p->n_ranks +
+             (uint64_t)rk * sbb + seg_off;
+    r.skip = false;
+    return r;
+  }
+};
+
 __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const ChunkCopyParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kTmaStages];
   const uint32_t tid = threadIdx.x;
+  // this CTA's contiguous share of the tiles
+  const uint64_t per = (p.total_tiles + gridDim.x - 1) / gridDim.x;
+  const uint64_t begin = (uint64_t)blockIdx.x * per;
+  const uint64_t end = begin + per < p.total_tiles ? begin + per : p.total_tiles;
   if (tid == 0) {
     for (int s = 0; s < kTmaStages; ++s)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&full_bar[s])));
@@ -197,7 +269,7 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const Chunk
   }
   __syncthreads();
   if (tid >= 32) {
-    // helper warps: header words (gather) and tiles the bulk engine cannot take
+    // helper warps: header words (gather) and the tiles the bulk engine cannot take
     const uint32_t h = tid - 32, nh = kTmaThreads - 32;
     if (p.to_blob && p.n_header_words) {
       const uint64_t total = (uint64_t)p.n_blobs * p.n_header_words;
@@ -207,8 +279,10 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const Chunk
         if (base) reinterpret_cast<uint32_t *>(base)[w] = p.header_words[w];
       }
     }
-    for (uint64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
-      const TileRef r = tile_ref(p, t);
+    TileCursor cur;
+    cur.init(&p, begin, end);
+    for (; cur.t < cur.end; cur.advance()) {
+      const TileRef r = cur.ref();
       if (r.skip || tma_ok(r)) continue;
       uint8_t *dst = p.to_blob ? r.blob : r.member;
       const uint8_t *src = p.to_blob ? r.member : r.blob;
@@ -223,43 +297,46 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const Chunk
   }
   if (tid != 0) return;
   const uint32_t smem_base = (uint32_t)__cvta_generic_to_shared(smem);
-  uint64_t k_load = 0, k_done = 0;  // positions in this CTA's list of bulk tiles
-  uint64_t t_load = blockIdx.x, t_done = blockIdx.x;  // tile cursors (skip non-bulk tiles)
-  auto next_bulk = [&](uint64_t t, TileRef *out) -> uint64_t {
-    for (; t < p.total_tiles; t += gridDim.x) {
-      const TileRef r = tile_ref(p, t);
+  TileRef ring[kTmaStages];  // tile of each stage, computed once at load time
+  TileCursor cur;
+  cur.init(&p, begin, end);
+  auto next_bulk = [&](TileRef *out) -> bool {
+    for (; cur.t < cur.end; cur.advance()) {
+      const TileRef r = cur.ref();
       if (!r.skip && tma_ok(r)) {
         *out = r;
-        return t;
+        cur.advance();
+        return true;
       }
     }
-    return p.total_tiles;
+    return false;
   };
-  TileRef rl{}, rd{};
-  t_load = next_bulk(t_load, &rl);
-  t_done = t_load;
-  rd = rl;
-  bool failed = false;
-  while (t_done < p.total_tiles && !failed) {
+  uint64_t k_load = 0, k_done = 0;
+  bool more = true, failed = false;
+  TileRef next{};
+  more = next_bulk(&next);
+  while ((more || k_done < k_load) && !failed) {
     // keep up to kTmaStages - 2 loads ahead of the tile being stored
-    while (t_load < p.total_tiles && k_load - k_done < (uint64_t)(kTmaStages - 2)) {
+    while (more && k_load - k_done < (uint64_t)(kTmaStages - 2)) {
       const int stage = (int)(k_load % kTmaStages);
       if (k_load >= (uint64_t)kTmaStages) {
-        // the store of tile k_load - kTmaStages (group k_load - kTmaStages) must have read the stage
+        // the store that last read this stage (group k_load - kTmaStages) must have read it
         const int64_t allowed = (int64_t)k_done - 1 - ((int64_t)k_load - kTmaStages);
         bulk_wait_read(allowed < 0 ? 0 : (int)allowed);
       }
       const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&full_bar[stage]);
       const uint32_t dst = smem_base + (uint32_t)stage * kTmaTile;
-      const uint8_t *src = p.to_blob ? rl.member : rl.blob;
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)rl.len) : "memory");
+      const uint8_t *src = p.to_blob ? next.member : next.blob;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"((uint32_t)next.len) : "memory");
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-          "l"(src), "r"((uint32_t)rl.len), "r"(bar)
+          "l"(src), "r"((uint32_t)next.len), "r"(bar)
           : "memory");
+      ring[stage] = next;
       ++k_load;
-      t_load = next_bulk(t_load + gridDim.x, &rl);
+      more = next_bulk(&next);
     }
+    if (k_done == k_load) break;
     const int stage = (int)(k_done % kTmaStages);
     const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&full_bar[stage]);
     if (!mbar_wait(bar, (uint32_t)((k_done / kTmaStages) & 1))) {
@@ -270,13 +347,13 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const Chunk
         mbar_wait((uint32_t)__cvta_generic_to_shared(&full_bar[j % kTmaStages]), (uint32_t)((j / kTmaStages) & 1));
       break;
     }
+    const TileRef &rd = ring[stage];
     uint8_t *dst = p.to_blob ? rd.blob : rd.member;
     asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
                  "r"(smem_base + (uint32_t)stage * kTmaTile), "r"((uint32_t)rd.len)
                  : "memory");
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     ++k_done;
-    t_done = next_bulk(t_done + gridDim.x, &rd);
   }
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
