@@ -216,6 +216,32 @@ int kvs_scatter_chunk(const void *blob, uint64_t blob_bytes, const uint64_t *mem
                       const uint64_t *member_extent, const uint32_t *block_ids,
                       uint32_t n_blocks, const uint64_t *region_bases, void *stream);
 
+/* ---- chunk gather for callers that cannot allocate ----
+ * No counterpart in the reference. Same arguments, validation and result as kvs_gather_chunk,
+ * but the per-call metadata (member pointers, block sizes, region bases, block ids, header words)
+ * is staged in one fixed device array compiled into the library instead of a buffer taken from
+ * the CUDA allocator, so the call makes no cudaMalloc / cudaMallocAsync / cudaFree or other
+ * allocating call. It exists for callers that must not allocate: serving engines that hand
+ * nearly all HBM to their paged KV pool and leave no headroom (or must keep their memory
+ * accounting exact), and latency-critical restore paths where an allocation could synchronise
+ * the device.
+ *   - Limit: the metadata must fit KVS_NOALLOC_SCRATCH_BYTES (8 x n_ranks x n_members
+ *     + 24 x n_members + 8 x n_blocks + 4 x n_header_words bytes, each part rounded up to 16,
+ *     about 64 KiB); larger requests fail with KVS_E_INVAL and a message naming the limit.
+ *   - Every GPU that loads the library holds the array (64 KiB) until the process exits.
+ *   - The first call on a device looks up the array's device address; make that first call
+ *     before any stream capture on that device.
+ *   - All calls share the array and each call overwrites it: calls whose work overlaps on the
+ *     GPU (different streams, or different host threads) race on it; issue them on one stream
+ *     or order them with events. */
+#define KVS_NOALLOC_SCRATCH_BYTES (64u * 1024u)
+int kvs_gather_chunk_noalloc(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_members,
+                             const uint64_t *member_block_bytes, const uint64_t *member_extent,
+                             const uint32_t *block_ids, uint32_t n_blocks,
+                             const uint64_t *region_bases, const uint32_t *header_words,
+                             uint32_t n_header_words, void *blob, uint64_t blob_bytes,
+                             void *stream);
+
 /* kernels launched by this library since load (a launch counter for the benchmark) */
 uint64_t kvs_kernel_launch_count(void);
 

@@ -121,4 +121,7 @@ inline uint32_t fnv1a32(const uint8_t *key, uint32_t len) {
 
 uint64_t kernel_launches();
 
+// Sets the thread-local message kvs_last_error() returns (defined with the C ABI).
+void set_last_error(const char *message);
+
 }  // namespace kvs

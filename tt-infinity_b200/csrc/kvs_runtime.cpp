@@ -831,6 +831,10 @@ size_t stage_value_copy(Staging &st, uint64_t dst, uint64_t src, uint64_t len) {
 
 }  // namespace
 
+namespace kvs {
+void set_last_error(const char *message) { g_err = message; }
+}  // namespace kvs
+
 // ============================================================================ C ABI
 
 extern "C" {

@@ -192,6 +192,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         C.c_int,
         [_u64p, C.c_uint32, C.c_uint32, _u64p, _u64p, _u32p, C.c_uint32, _u64p, _u32p, C.c_uint32, P, C.c_uint64, P],
     ),
+    "kvs_gather_chunk_noalloc": (
+        C.c_int,
+        [_u64p, C.c_uint32, C.c_uint32, _u64p, _u64p, _u32p, C.c_uint32, _u64p, _u32p, C.c_uint32, P, C.c_uint64, P],
+    ),
     "kvs_scatter_chunk": (
         C.c_int,
         [P, C.c_uint64, _u64p, C.c_uint32, C.c_uint32, _u64p, _u64p, _u32p, C.c_uint32, _u64p, P],
