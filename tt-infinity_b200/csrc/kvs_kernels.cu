@@ -341,6 +341,7 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const Chunk
     const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&full_bar[stage]);
     if (!mbar_wait(bar, (uint32_t)((k_done / kTmaStages) & 1))) {
       atomicAdd(&g_tma_timeouts, 1u);
+      if (p.timeout_flag) *reinterpret_cast<volatile unsigned int *>(p.timeout_flag) = 1u;
       failed = true;
       // give the loads still in flight a bounded chance to land before the CTA exits
       for (uint64_t j = k_done + 1; j < k_load; ++j)

@@ -68,6 +68,7 @@ struct ChunkCopyParams {
   uint64_t tiles_per_combo;  // tile_prefix[n_members]
   uint64_t total_tiles;
   int to_blob;               // 1: members -> blob (gather), 0: blob -> members (scatter)
+  unsigned int *timeout_flag;  // optional host-mapped word set to 1 if a bounded wait expires
 };
 
 struct LookupParams {

@@ -84,6 +84,7 @@ struct DeviceGuard {
 // Growable pinned host + device staging area. One upload per call.
 struct Staging {
   uint8_t *host = nullptr;
+  uint8_t *host_dev = nullptr;  // device alias of the mapped host buffer (kernels write results here)
   uint8_t *dev = nullptr;
   size_t cap = 0, used = 0;
   cudaEvent_t uploaded = nullptr;  // last upload out of `host` finished
@@ -104,7 +105,8 @@ struct Staging {
       dev = nullptr;
       size_t c = std::max<size_t>(need, 1 << 20);
       c = (c + 4095) & ~size_t(4095);
-      CUDA_TRY(cudaMallocHost(&host, c));
+      CUDA_TRY(cudaHostAlloc(reinterpret_cast<void **>(&host), c, cudaHostAllocMapped | cudaHostAllocPortable));
+      CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void **>(&host_dev), host, 0));
       CUDA_TRY(cudaMalloc(&dev, c));
       cap = c;
     }
@@ -127,6 +129,7 @@ struct Staging {
   }
   template <class T> T *h(size_t off) { return reinterpret_cast<T *>(host + off); }
   template <class T> T *d(size_t off) { return reinterpret_cast<T *>(dev + off); }
+  template <class T> T *hd(size_t off) { return reinterpret_cast<T *>(host_dev + off); }
   int upload(cudaStream_t stream, size_t bytes) {
     if (bytes) CUDA_TRY(cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, stream));
     CUDA_TRY(cudaEventRecord(uploaded, stream));
@@ -185,6 +188,7 @@ struct kvs_server {
   kvs::DevMeta *d_meta = nullptr;
   uint32_t *d_keyrows = nullptr;
   uint8_t *pool = nullptr;
+  uint8_t *pool_dev = nullptr;  // device alias of the mapped pool
   cudaStream_t wt_stream = nullptr;
   cudaEvent_t tail = nullptr;  // newest event of the shard's ordering chain (not owned)
   std::vector<WtBatch> wt_batches;
@@ -233,6 +237,16 @@ struct kvs_server {
   }
   uint8_t *host_ptr(const HostBacking &b) const {
     return b.in_pool ? pool + b.pool_unit * cfg.unit_bytes : b.heap;
+  }
+  // device alias of a host backing, for kernels that read the host tier directly over PCIe
+  uint64_t device_alias(const HostBacking &b) const {
+    if (b.in_pool) return reinterpret_cast<uint64_t>(pool_dev) + b.pool_unit * cfg.unit_bytes;
+    void *d = nullptr;
+    if (cudaHostGetDevicePointer(&d, b.heap, 0) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    return reinterpret_cast<uint64_t>(d);
   }
   int reserve_backing(uint64_t len, HostBacking *out) {
     HostBacking b;
@@ -318,6 +332,7 @@ struct kvs_client {
   kvs_put_profile prof{};
   std::vector<uint64_t> validated_members;
   // kernel timing (events around copy-engine launches)
+  unsigned int *timeout_flag = nullptr;  // host-mapped word a copy kernel sets if a bounded wait expires
   bool timing = false;
   struct Timed {
     cudaEvent_t start, stop;
@@ -376,17 +391,18 @@ bool tma_enabled() {
   return on;
 }
 
-cudaError_t launch_copy(const kvs::ChunkCopyParams &p, cudaStream_t stream, bool device_memory_only) {
+cudaError_t launch_copy(kvs::ChunkCopyParams p, cudaStream_t stream, bool device_memory_only,
+                        unsigned int *timeout_flag) {
+  p.timeout_flag = timeout_flag;
   if (device_memory_only && tma_enabled()) return kvs::launch_chunk_copy_tma(p, stream);
   return kvs::launch_chunk_copy(p, stream);
 }
 
 // Bounded waits in the bulk engine that expired (never in normal operation) turn into an error.
-int check_tma_timeouts(const char *op) {
-  unsigned int n = 0;
-  cudaError_t e = kvs::read_tma_timeouts(&n);
-  if (e != cudaSuccess) return set_err(KVS_E_CUDA, "%s: reading the copy-engine status: %s", op, cudaGetErrorString(e));
-  if (n) return set_err(KVS_E_TIMEOUT, "%s: %u copy-engine waits expired", op, n);
+// The kernel sets the client's host-mapped flag, read here after the call synchronised.
+int check_tma_timeouts(kvs_client *c, const char *op) {
+  if (c->timeout_flag && *reinterpret_cast<volatile unsigned int *>(c->timeout_flag))
+    return set_err(KVS_E_TIMEOUT, "%s: copy-engine waits expired", op);
   return KVS_OK;
 }
 
@@ -690,7 +706,7 @@ int flush_puts(PutBatch &b, cudaStream_t) {
       p.to_blob = 1;
       cudaEvent_t t0 = nullptr;
       c->time_begin(&t0);
-      CUDA_TRY(launch_copy(p, c->stream, true));
+      CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
       c->time_end(t0, 0, (uint64_t)n * (b.fmt->value_len - 4ull * b.fmt->header.size()));
     } else {
       for (size_t i = 0; i < n; ++i) {
@@ -710,7 +726,7 @@ int flush_puts(PutBatch &b, cudaStream_t) {
         p.tiles_per_combo = (b.items[i].len + kTileBytes - 1) / kTileBytes;
         p.total_tiles = p.tiles_per_combo;
         p.to_blob = 1;
-        CUDA_TRY(launch_copy(p, c->stream, true));
+        CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
       }
     }
     for (size_t i = 0; i < ns; ++i)
@@ -812,7 +828,7 @@ int launch_value_copy(kvs_client *c, uint64_t dst, uint64_t src, uint64_t len, s
   p.to_blob = 0;
   (void)dst;
   (void)src;
-  CUDA_TRY(launch_copy(p, c->stream, dst != 0));
+  CUDA_TRY(launch_copy(p, c->stream, dst != 0, c->timeout_flag));
   return KVS_OK;
 }
 
@@ -918,6 +934,8 @@ int kvs_server_create(const kvs_server_config *cfg_in, kvs_server **out) {
     const uint64_t bytes = (cfg.host_pool_bytes / cfg.unit_bytes) * cfg.unit_bytes;
     if ((e = cudaHostAlloc(&s->pool, bytes, cudaHostAllocPortable | cudaHostAllocMapped)) != cudaSuccess)
       return fail(set_err(KVS_E_NOSPACE, "host pool of %llu B: %s", (unsigned long long)bytes, cudaGetErrorString(e)));
+    if ((e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&s->pool_dev), s->pool, 0)) != cudaSuccess)
+      return fail(set_err(KVS_E_CUDA, "host pool device alias: %s", cudaGetErrorString(e)));
   }
   if ((e = cudaStreamCreateWithFlags(&s->wt_stream, cudaStreamNonBlocking)) != cudaSuccess)
     return fail(set_err(KVS_E_CUDA, "write-through stream: %s", cudaGetErrorString(e)));
@@ -1117,6 +1135,9 @@ int kvs_client_create(kvs_server *const *shards, uint32_t n_shards, int32_t devi
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->entry_evt, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->exit_evt, cudaEventDisableTiming);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->landed_evt, cudaEventDisableTiming);
+  if (e == cudaSuccess)
+    e = cudaHostAlloc(reinterpret_cast<void **>(&c->timeout_flag), 64, cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e == cudaSuccess) *c->timeout_flag = 0;
   c->chain_evt.assign(n_shards, nullptr);
   for (uint32_t i = 0; i < n_shards && e == cudaSuccess; ++i)
     e = cudaEventCreateWithFlags(&c->chain_evt[i], cudaEventDisableTiming);
@@ -1155,6 +1176,7 @@ int kvs_client_destroy(kvs_client *c) {
     c->closed = true;
     c->drain_timing();
     for (auto e : c->event_pool) cudaEventDestroy(e);
+    if (c->timeout_flag) cudaFreeHost(c->timeout_flag);
     c->stage.release();
     for (auto e : c->chain_evt)
       if (e) cudaEventDestroy(e);
@@ -1286,7 +1308,7 @@ int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_
   PackedMutations pm = pack_mutations(s, c->stage);
   uint64_t src;
   if (action == Directory::GetAction::kHostOnly)
-    src = reinterpret_cast<uint64_t>(s->host_ptr(hb));  // mapped pinned memory, read over PCIe
+    src = s->device_alias(hb);  // mapped pinned memory, read over PCIe
   else
     src = s->slab_base() + e.value_off;
   const size_t rec = stage_value_copy(c->stage, reinterpret_cast<uint64_t>(out), src, len);
@@ -1299,7 +1321,7 @@ int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_
   s->launches++;
   TRY(chain_record(c, si));
   CUDA_TRY(cudaStreamSynchronize(c->stream));
-  TRY(quarantine_on_error(c, check_tma_timeouts("get")));
+  TRY(quarantine_on_error(c, check_tma_timeouts(c, "get")));
   if (action != Directory::GetAction::kDevice) {
     s->mprof.to_device_count++;
     s->moves_completed.fetch_add(1, std::memory_order_relaxed);
@@ -1590,7 +1612,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     if (inv[i]) TRY(chain_wait(c, c->shards[i]));
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms[i])));
-  TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.d<kvs::LookupOut>(out_off),
+  TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.hd<kvs::LookupOut>(out_off),
                                             st.d<uint64_t>(blob_off), fmt.value_len)));
   kvs::ChunkCopyParams p{};
   p.member_ptrs = st.d<uint64_t>(mp_off);
@@ -1611,19 +1633,17 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
   for (uint32_t m = 0; m < layout->n_members; ++m) payload_per_block += layout->member_block_bytes[m];
   cudaEvent_t t0 = nullptr;
   c->time_begin(&t0);
-  CUDA_TRY(launch_copy(p, c->stream, true));
+  CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
   c->time_end(t0, 1, (uint64_t)n * payload_per_block);  // misses copy nothing; corrected below
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) c->shards[i]->launches++;
-  CUDA_TRY(cudaMemcpyAsync(st.h<kvs::LookupOut>(out_off), st.d<kvs::LookupOut>(out_off), sizeof(kvs::LookupOut) * n,
-                           cudaMemcpyDeviceToHost, c->stream));
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) TRY(chain_record(c, i));
   // while the GPU works: the authoritative host lookups
   std::vector<uint32_t> host_slot(n);
   for (uint32_t i = 0; i < n; ++i) host_slot[i] = c->shards[si[i]]->dir->lookup((const uint8_t *)&keys[i], 8);
   CUDA_TRY(cudaStreamSynchronize(c->stream));
-  TRY(quarantine_on_error(c, check_tma_timeouts("get_blocks")));
+  TRY(quarantine_on_error(c, check_tma_timeouts(c, "get_blocks")));
   std::vector<kvs::LookupOut> res(n);
   for (uint32_t j = 0; j < n; ++j) res[ord.perm[j]] = st.h<kvs::LookupOut>(out_off)[j];
   int format_error = -1;
@@ -1648,6 +1668,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     const uint8_t *host;
     uint64_t len;
     bool scatter;  // pass 1 did not deliver it (host-tier hit)
+    uint64_t host_dev;  // device alias of the host copy
   };
   std::vector<Late> late;
   std::map<std::pair<uint32_t, uint32_t>, size_t> admitted;  // (shard, slot) -> index in late
@@ -1669,7 +1690,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     if (action == Directory::GetAction::kDevice) continue;
     const HostBacking &hb = s->dir->backing(host_slot[i]);
     Late L{i, si[i], host_slot[i], 0, s->host_ptr(hb), s->dir->entry(host_slot[i]).total_len,
-           res[i].status == kvs::kHitHost};
+           res[i].status == kvs::kHitHost, s->device_alias(hb)};
     if (action == Directory::GetAction::kAdmit) {
       L.admit_dst = s->slab_base() + off;
       admitted[{si[i], host_slot[i]}] = late.size();
@@ -1693,7 +1714,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     for (auto &L : late)
       if (L.scatter) {
         // admitted values are scattered from their new slab block, others from host memory
-        st.h<uint64_t>(blobs2)[k] = L.admit_dst ? L.admit_dst : reinterpret_cast<uint64_t>(L.host);
+        st.h<uint64_t>(blobs2)[k] = L.admit_dst ? L.admit_dst : L.host_dev;
         st.h<int64_t>(ids2)[k] = block_ids[L.i];
         ++k;
       }
@@ -1720,7 +1741,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
       q.blob_ptrs = st.d<uint64_t>(blobs2);
       q.n_blobs = (uint32_t)nscatter;
       q.total_tiles = (uint64_t)nscatter * q.tiles_per_combo;
-      CUDA_TRY(launch_copy(q, c->stream, false));
+      CUDA_TRY(launch_copy(q, c->stream, false, c->timeout_flag));
     }
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) TRY(chain_record(c, i));
@@ -1771,9 +1792,7 @@ int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *f
     if (inv[i]) TRY(chain_wait(c, c->shards[i]));
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms[i])));
-  TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.d<kvs::LookupOut>(out_off), nullptr, 0)));
-  CUDA_TRY(cudaMemcpyAsync(st.h<kvs::LookupOut>(out_off), st.d<kvs::LookupOut>(out_off), sizeof(kvs::LookupOut) * n,
-                           cudaMemcpyDeviceToHost, c->stream));
+  TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.hd<kvs::LookupOut>(out_off), nullptr, 0)));
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) TRY(chain_record(c, i));
   CUDA_TRY(cudaStreamSynchronize(c->stream));
@@ -1917,7 +1936,7 @@ static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_me
   p.tiles_per_combo = tile_prefix[n_members];
   p.total_tiles = (uint64_t)n_blocks * n_ranks * p.tiles_per_combo;
   p.to_blob = to_blob;
-  CUDA_TRY(launch_copy(p, s, true));
+  CUDA_TRY(launch_copy(p, s, true, nullptr));
   CUDA_TRY(cudaFreeAsync(dbuf, s));
   // the host buffer was consumed by a pageable copy, which completes before returning
   return KVS_OK;
