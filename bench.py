@@ -58,6 +58,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency-samples", type=int, default=40)
+    ap.add_argument("--sweep", action="store_true",
+                    help="fp8 + per-block-scale layout, batches of 1..4096 blocks (prints a sweep table)")
+    ap.add_argument("--multiturn", action="store_true",
+                    help="32 sessions x 5 turns of prefix reuse with a slab of 25%% of the working set")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: 16 layers, 512-block pool, 64 blocks per step (same kernels)")
     args = ap.parse_args()
@@ -447,8 +451,170 @@ def run_reference(args, rank, world):
     }
 
 
+# ------------------------------------------------------------------ fp8 batch sweep (latency vs bandwidth)
+
+FP8_LAYERS, FP8_HEADS, FP8_DIM, FP8_BLOCK_TOKENS = 80, 8, 128, 16
+FP8_POOL_BLOCKS = 32768  # 65,536 blocks (160 GiB) do not fit next to a slab; half the pool is used
+
+
+def fp8_layout(torch, device, pool_blocks):
+    """Per layer: K and V fp8 e4m3 (pool_blocks, 8, 16, 128) and one fp32 scale per block."""
+    from kvcache_manager import PagedLayout
+
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    members = []
+    for _ in range(FP8_LAYERS):
+        for _ in range(2):
+            t = torch.empty((pool_blocks, FP8_HEADS, FP8_BLOCK_TOKENS, FP8_DIM), dtype=torch.uint8, device=device)
+            t.random_(0, 256, generator=g)
+            members.append(t.view(torch.float8_e4m3fn))
+        members.append(torch.rand((pool_blocks,), generator=g, device=device))
+    return PagedLayout(members, members_per_layer=3)
+
+
+def run_sweep(args):
+    """put (landed) and get (device hit) GB/s and per-call latency for batches of 1..4096 blocks."""
+    import torch
+
+    from kvcache_manager import Client, Server, codec
+
+    torch.cuda.set_device(0)
+    layout = fp8_layout(torch, 0, FP8_POOL_BLOCKS)
+    vlen = layout.value_bytes()
+    payload = sum(layout.member_block_bytes)
+    units = -(-vlen // UNIT_BYTES)
+    block_units = 1 << (units - 1).bit_length()
+    server = Server(0, max_keys=2 * 4096 + 64, heap_bytes=(4096 + 64) * block_units * UNIT_BYTES,
+                    host_pool_bytes=(4096 + 64) * units * UNIT_BYTES)
+    client = Client(0, server)
+    rng = np.random.default_rng(9)
+    rows = []
+    for batch in [1, 4, 16, 64, 256, 1024, 4096]:
+        put_ms, get_ms = [], []
+        reps = max(2, min(20, 2048 // batch))
+        for r in range(reps + 1):
+            perm = rng.permutation(FP8_POOL_BLOCKS)
+            keys = np.array(codec.chained_block_hashes(batch * 1000 + r, batch), np.uint64)
+            src, dst = perm[:batch], perm[batch:2 * batch]
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            client.put_blocks(layout, keys, src)
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+            client.flush()
+            torch.cuda.synchronize()
+            t2 = time.perf_counter()
+            found = client.get_blocks(layout, keys, dst)
+            torch.cuda.synchronize()
+            t3 = time.perf_counter()
+            assert found.all()
+            for k in keys:  # keep the catalog bounded
+                client.delete(int(k))
+            if r:
+                put_ms.append((t1 - t0) * 1e3)
+                get_ms.append((t3 - t2) * 1e3)
+        p50p, p50g = statistics.median(put_ms), statistics.median(get_ms)
+        rows.append({"blocks": batch, "bytes": batch * payload,
+                     "put_landed_ms_p50": round(p50p, 4), "put_landed_GBps": round(batch * payload / p50p / 1e6, 2),
+                     "get_ms_p50": round(p50g, 4), "get_ms_p99": round(sorted(get_ms)[-1], 4),
+                     "get_GBps": round(batch * payload / p50g / 1e6, 2), "reps": reps})
+    client.close()
+    server.close()
+    return {"sweep": "fp8 e4m3 KV + fp32 per-block scales, 80 layers x 8 heads x 128 dim, 16-token blocks",
+            "pool_blocks": FP8_POOL_BLOCKS, "bytes_per_block": payload, "value_bytes": vlen,
+            "note": "put = landed (gather into the slab, write-through then flushed outside the put time); get = "
+                    "device-tier hit; wall clock around the Python API call",
+            "rows": rows}
+
+
+# ------------------------------------------------------------------ multi-turn prefix reuse (config-1 shape)
+
+def multiturn_plan(n_sessions, n_turns, seed=3, lo=512, hi=4096, block_tokens=32):
+    """Per session and turn: the prompt's full-block count; each turn extends the prior conversation."""
+    rng = np.random.default_rng(seed)
+    plan = []
+    for s in range(n_sessions):
+        total, turns = 0, []
+        for t in range(n_turns):
+            total += int(rng.integers(lo, hi + 1))
+            turns.append(total // block_tokens)
+        plan.append(turns)
+    return plan
+
+
+def run_multiturn_workload(client, layout, plan, pool_blocks, seed=3, on_turn=None):
+    """Each turn: exists on the prompt's blocks, get the longest contiguous prefix of hits, put the
+    rest. Block keys are chained prefix hashes per session, so turn t+1 shares turn t's prefix."""
+    from kvcache_manager import codec
+
+    rng = np.random.default_rng(seed + 1)
+    stats = {"blocks": 0, "prefix_hits": 0, "puts": 0, "gets": 0}
+    order = [(t, s) for t in range(len(plan[0])) for s in range(len(plan))]  # sessions interleave by turn
+    for t, s in order:
+        n = plan[s][t]
+        keys = np.array(codec.chained_block_hashes(1_000_003 * (s + 1), n), np.uint64)
+        found = client.exists_batch(keys)
+        hit = int(np.argmin(found)) if not found.all() else n
+        slots = rng.permutation(pool_blocks)[:n]
+        if hit:
+            got = client.get_blocks(layout, keys[:hit], slots[:hit])
+            assert got.all(), "a prefix block reported by exists was not restored"
+        if hit < n:
+            client.put_blocks(layout, keys[hit:], slots[hit:])
+        stats["blocks"] += n
+        stats["prefix_hits"] += hit
+        stats["gets"] += hit
+        stats["puts"] += n - hit
+        if on_turn:
+            on_turn(t, s, keys, hit, slots)
+    return stats
+
+
+def run_multiturn(args):
+    import torch
+
+    from kvcache_manager import Client, PagedLayout, Server
+
+    torch.cuda.set_device(0)
+    layers, heads, dim, bt, pool = 2, 8, 128, 32, 1024
+    g = torch.Generator(device=0)
+    g.manual_seed(7)
+    kv = [tuple(torch.empty((pool, heads, bt, dim), dtype=torch.bfloat16, device=0).normal_(generator=g)
+                for _ in range(2)) for _ in range(layers)]
+    layout = PagedLayout.from_kv_caches(kv)
+    plan = multiturn_plan(32, 5)
+    working_set = sum(p[-1] for p in plan)  # distinct blocks the sessions produce
+    vlen = layout.value_bytes()
+    units = -(-vlen // UNIT_BYTES)
+    block_bytes = (1 << (units - 1).bit_length()) * UNIT_BYTES
+    slab = max(block_bytes, working_set * block_bytes // 4)  # 25 % of the working set
+    server = Server(0, max_keys=2 * working_set, heap_bytes=slab, host_pool_bytes=(working_set + 64) * units * UNIT_BYTES)
+    client = Client(0, server)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    st = run_multiturn_workload(client, layout, plan, pool)
+    client.flush()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    sst = server.stats()
+    client.close()
+    server.close()
+    payload = sum(layout.member_block_bytes)
+    return {"multiturn": "32 sessions x 5 turns, U(512, 4096) tokens per turn, config-1 KV shape, slab = 25% of the working set",
+            "working_set_blocks": working_set, "slab_bytes": slab, "wall_s": round(dt, 3),
+            "blocks_restored": st["gets"], "blocks_put": st["puts"],
+            "prefix_hit_rate": round(st["prefix_hits"] / max(1, st["blocks"]), 4),
+            "host_tier_serves": sst["host_serves"], "admissions": sst["admissions"],
+            "victims_evicted": sst["victims_evicted"],
+            "moved_GBps": round((st["gets"] + st["puts"]) * payload / dt / GB, 3)}
+
+
 def main():
     args = parse()
+    if args.sweep or args.multiturn:
+        print(json.dumps(run_sweep(args) if args.sweep else run_multiturn(args)))
+        return
     rank, local_rank, world = dist_env()
     if world != args.gpus and world == 1 and args.gpus > 1:
         print(json.dumps({"error": "run N>1 under torchrun (one rank per GPU)"}))
