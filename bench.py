@@ -500,7 +500,7 @@ def run_sweep(args):
             torch.cuda.synchronize()
             t0 = time.perf_counter()
             client.put_blocks(layout, keys, src)
-            torch.cuda.synchronize()
+            torch.cuda.current_stream().synchronize()  # landed: the caller's stream, not the write-through
             t1 = time.perf_counter()
             client.flush()
             torch.cuda.synchronize()
