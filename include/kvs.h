@@ -196,6 +196,61 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n,
 /* EXISTS over a batch of 64-bit keys through the device index; no recency update. */
 int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found);
 
+/* ---- hash sharding across processes (one process per GPU) ----
+ * The reference serves several server worker groups behind one Fabric endpoint
+ * (src/native/ttnn/server_runtime/server.cpp:80-86), each an independent directory; here each
+ * shard is a process on its own GPU and the block bytes cross NVLink as kernel-issued P2P
+ * stores. A step is bulk-synchronous (the host exchange runs on torch.distributed):
+ *   1. clients send get and put keys to the owning shards;
+ *   2. the owner serves the gets: lookup, then one scatter launch that stores each hit
+ *      straight into the requesting process's paged pool (opened from IPC handles);
+ *   3. the owner grants the puts (slab offsets), the clients gather their blocks straight into
+ *      the owners' slabs, and after every client's copy has finished each owner starts the host
+ *      write-through of what landed.
+ * None of these has a counterpart entry point in the reference, whose shards share one process. */
+typedef struct {
+  uint8_t bytes[64];
+} kvs_ipc_handle; /* a cudaIpcMemHandle_t */
+
+/* IPC handle of the device allocation holding `ptr`, and ptr's offset inside it */
+int kvs_ipc_export(const void *ptr, kvs_ipc_handle *handle, uint64_t *offset);
+/* map another process's allocation on `device` (peer access enabled on first use) */
+int kvs_ipc_open(int32_t device, const kvs_ipc_handle *handle, void **base);
+int kvs_ipc_close(int32_t device, void *base);
+/* the shard's value slab (a device allocation of its own, so its IPC offset is 0) */
+int kvs_server_slab(kvs_server *s, void **base, uint64_t *bytes);
+
+/* Owner side (a client whose only shard is the owner's). Gets of several requesters in one
+ * call: key i is scattered into the paged pool layouts[sets[i]], whose member pointers may be
+ * peer memory. Same semantics as kvs_get_blocks on the concatenated batch; every layout must
+ * have the same member sizes. n == 0 still runs the commit barrier. */
+int kvs_serve_gets(kvs_client *c, uint32_t n_sets, const kvs_block_layout *layouts, uint32_t n,
+                   const uint32_t *sets, const int64_t *block_ids, const uint64_t *keys, uint8_t *found,
+                   void *stream);
+/* Owner side: the same gets delivered as whole values (header included), value i into
+ * rows + i * value_len (this GPU's memory), for transports that move contiguous buffers. */
+int kvs_serve_gets_packed(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *keys,
+                          uint8_t *found, void *stream);
+/* Owner side: publish puts in order (pending, pinned), returning each value's slab offset.
+ * Stops early (n_granted < n) at a put whose space needs the host commit of a value that has
+ * not landed yet; the rest are granted after kvs_puts_landed. KVS_E_NOSPACE if a value can
+ * never fit. */
+int kvs_grant_puts(kvs_client *c, uint32_t n, const uint64_t *keys, uint64_t value_len, uint64_t *slab_offsets,
+                   uint32_t *n_granted);
+/* Owner side: every granted value has been written (ordered before `stream`'s current work);
+ * start their host write-through. */
+int kvs_puts_landed(kvs_client *c, void *stream);
+
+/* Client side: one copy launch between the layout's blocks (this GPU's memory) and explicit
+ * value addresses (this GPU's or a peer's); to_blob 1 gathers (writes the value header too),
+ * 0 scatters. Addresses are 16-byte aligned; a zero address skips the block. */
+int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const int64_t *block_ids,
+                    const uint64_t *blob_addrs, int to_blob, void *stream);
+/* One copy launch between whole values at explicit addresses and contiguous rows:
+ * to_rows 1 copies addrs[i] -> rows + i * value_len, 0 the reverse. */
+int kvs_copy_values(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *addrs, int to_rows,
+                    void *stream);
+
 /* ---- chunk gather / scatter ops ----
  * gather_tp_shards_to_chip / pack_local_shards (patch 0003 gather.hpp lines 9372-9417) and
  * their inverses scatter_chunk_from_chip / unpack_local_shards (9418-9453).

@@ -1018,6 +1018,9 @@ static int put_one(kvo_store *s, const uint8_t *key, uint32_t key_len, const uin
                   (unsigned long long)len);
     flush_copies(s);
     commit_fifo_head(s); /* force_put_host_commit, then retry the prepare */
+    /* force_put_host_commit returns after the head's host copy has landed: the retry may evict
+     * the value just committed and hand its block to this put */
+    flush_copies(s);
   }
 }
 

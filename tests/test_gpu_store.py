@@ -260,9 +260,12 @@ def test_directory_policy_matches_oracle_under_pressure(store, seed):
     assert np.array_equal(dev_b[:, 1], host_b[:, 1]) and np.array_equal(dev_b[live, 0], host_b[live, 0])
 
 
-def test_block_path_eviction_and_host_tier_matches_oracle(store):
+@pytest.mark.parametrize("repeat_keys", [False, True])
+def test_block_path_eviction_and_host_tier_matches_oracle(store, repeat_keys):
     """Blocks under a slab that holds a quarter of them: LRU eviction, host-tier serves and
-    read-through admissions on get_blocks, compared with the oracle's sequential semantics."""
+    read-through admissions on get_blocks, compared with the oracle's sequential semantics. With
+    repeat_keys a get batch names some keys more than once (a host-tier key admitted by its first
+    get is read from its new block by the later ones)."""
     n_layers, heads, bs, dim, pool = 2, 2, 16, 64, 96
     kv = kv_pool(n_layers, heads, bs, dim, pool, seed=7)
     layout = PagedLayout.from_kv_caches(kv)
@@ -282,7 +285,7 @@ def test_block_path_eviction_and_host_tier_matches_oracle(store):
         src = rng.choice(48, 8, replace=False)
         c.put_blocks(layout, keys[idx], src)
         o.put_blocks(host, mb, keys[idx], src)
-        g = rng.choice(48, 12, replace=False)
+        g = rng.choice(48, 12, replace=repeat_keys)
         dst = 48 + rng.choice(48, 12, replace=False)
         fo = o.get_blocks(host, mb, keys[g], dst)
         fs = c.get_blocks(layout, keys[g], dst)

@@ -184,3 +184,22 @@ def test_block_path_under_eviction_serves_host_tier_bytes():
                     assert np.array_equal(host[m][d * seg:(d + 1) * seg], truth[int(k)][m])
     st = s.stats()
     assert st["admissions"] > 0 and st["victims_evicted"] > 0
+
+
+def test_forced_commit_lands_the_host_copy_before_its_block_is_reused():
+    """A put batch larger than the slab: the forced commit's host copy must be complete before the
+    retry evicts that value and reuses its block for the next put of the batch."""
+    seg, pool = 1024, 8
+    mb = [seg] * 2
+    _, _, vlen = O.block_format(mb)
+    units = -(-vlen // U)
+    s = O.Store(max_keys=16, heap_bytes=2 * (1 << (units - 1).bit_length()) * U, host_pool_bytes=1 << 20)
+    rng = np.random.default_rng(3)
+    host = [rng.integers(0, 256, pool * seg, dtype=np.uint8) for _ in range(2)]
+    keys = np.array([11, 22, 33], np.uint64)
+    s.put_blocks(host, mb, keys, [0, 1, 2])  # the third put forces a commit of the first and evicts it
+    assert s.location(11)[0] == 1  # host only
+    found = s.get_blocks(host, mb, keys[:1], [5])
+    assert found.all()
+    for m in range(2):
+        assert np.array_equal(host[m][5 * seg:6 * seg], host[m][0:seg])

@@ -1,0 +1,99 @@
+"""The collective protocol of the process-per-GPU sharded store on CPU gloo ranks: routing of
+requests and replies, the row transport, multi-round put grants and the per-step order (gets of
+every rank, then puts of every rank) must reproduce one oracle store per shard exactly."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from kvcache_manager import sharded
+from sharded_common import HostEngine, make_plan, make_pools, replay
+
+MB = 512  # bytes of one member block
+N_MEMBERS = 4
+N_POOL = 96
+CFG = dict(max_keys=48, heap_bytes=40 * 4288, host_pool_bytes=256 * 4288)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, steps, batch, grant_limit, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        plan = make_plan(world, steps, N_POOL, batch, seed=11)
+        pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=3)
+        eng = HostEngine(pools[rank], MB, CFG, grant_limit=grant_limit)
+        store = sharded.ShardedStore(eng, max_batch=batch, transport="nccl")
+        found = []
+        for row in plan:
+            gk, gi, pk, pi = row[rank]
+            found.append(store.step(gk, gi, pk, pi))
+        ex = store.exists_batch(plan[-1][rank][2])
+        store.flush()
+        q.put((rank, [m.copy() for m in eng.members], found, eng.stats(), ex, eng.rounds))
+        store.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,grant_limit", [(2, None), (3, 2)])
+def test_sharded_protocol_matches_per_shard_oracle(world, grant_limit):
+    steps, batch = 6, 12
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, batch, grant_limit, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = sorted((q.get(timeout=240) for _ in range(world)), key=lambda o: o[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    plan = make_plan(world, steps, N_POOL, batch, seed=11)
+    pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=3)
+    exp_pools, exp_found, exp_stats = replay(plan, pools, MB, CFG)
+    for rank, members, found, stats, ex, rounds in out:
+        for m in range(N_MEMBERS):
+            assert np.array_equal(members[m], exp_pools[rank][m]), f"rank {rank} member {m}"
+        for s in range(steps):
+            assert np.array_equal(found[s], exp_found[s][rank]), f"rank {rank} step {s}"
+        for f in ("live_keys", "device_resident_keys", "victims_evicted", "host_serves", "admissions",
+                  "writes_through", "epoch"):
+            assert stats[f] == exp_stats[rank][f], (rank, f)
+        assert ex.all()  # every key this rank put in the last step exists somewhere
+        if grant_limit:
+            assert rounds > steps  # some steps took more than one grant round
+    assert any(f.any() for fs in exp_found for f in fs) and not all(f.all() for fs in exp_found for f in fs)
+
+
+def test_pack_unpack_requests_round_trip():
+    world, cap = 3, 8
+    rng = np.random.default_rng(1)
+    gk = rng.integers(0, 2**63, 7).astype(np.uint64)
+    pk = rng.integers(0, 2**63, 5).astype(np.uint64)
+    gi, pi = np.arange(7), np.arange(10, 15)
+    rec, g_pos, p_pos = sharded.pack_requests(world, cap, 0, gk, gi, pk, pi)
+    for o in range(world):
+        (k, i, k2, i2), = sharded.unpack_requests(rec[o:o + 1], cap)
+        assert np.array_equal(k, gk[g_pos[o]]) and np.array_equal(i, gi[g_pos[o]])
+        assert np.array_equal(k2, pk[p_pos[o]]) and np.array_equal(i2, pi[p_pos[o]])
+        assert (sharded.shard_of_u64(k, world) == o).all()
+
+
+def test_shard_of_u64_matches_the_c_abi_function():
+    from kvcache_manager import dist as kdist
+
+    keys = np.random.default_rng(2).integers(0, 2**64 - 1, 300, dtype=np.uint64)
+    for n in (1, 2, 3, 8):
+        assert sharded.shard_of_u64(keys, n).tolist() == [kdist.shard_of(int(k), n) for k in keys]

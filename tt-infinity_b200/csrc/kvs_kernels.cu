@@ -58,6 +58,13 @@ __device__ __forceinline__ void cta_copy(uint8_t *dst, const uint8_t *src, uint6
   }
 }
 
+// Index of (blob, rank, member) in member_ptrs: blobs of member set s use the s-th group of
+// n_ranks x n_members pointers (several requesters' paged pools in one launch).
+__device__ __forceinline__ uint64_t member_index(const ChunkCopyParams &p, uint32_t blob, uint32_t rank, uint32_t m) {
+  const uint64_t set = p.blob_sets ? p.blob_sets[blob] : 0;
+  return (set * p.n_ranks + rank) * p.n_members + m;
+}
+
 __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const ChunkCopyParams p) {
   // Header words: one thread per (blob, word) -- gather only.
   if (p.to_blob && p.n_header_words) {
@@ -91,7 +98,7 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const ChunkCop
     const uint64_t seg_off = tile_in_seg * p.tile_bytes;
     const uint64_t len = (sbb - seg_off) < p.tile_bytes ? (sbb - seg_off) : p.tile_bytes;
     const int64_t block = p.block_ids[(uint64_t)blob * p.blocks_per_blob + cb];
-    uint8_t *member = reinterpret_cast<uint8_t *>(p.member_ptrs[(uint64_t)r * p.n_members + m]) +
+    uint8_t *member = reinterpret_cast<uint8_t *>(p.member_ptrs[member_index(p, blob, r, m)]) +
                       (uint64_t)block * sbb + seg_off;
     uint8_t *blob_ptr = reinterpret_cast<uint8_t *>(blob_base) + p.region_bases[m] +
                         (uint64_t)cb * sbb * p.n_ranks + (uint64_t)r * sbb + seg_off;
@@ -126,38 +133,6 @@ struct TileRef {
   uint64_t len;
   bool skip;
 };
-
-__device__ __forceinline__ TileRef tile_ref(const ChunkCopyParams &p, uint64_t t) {
-  TileRef r{};
-  const uint64_t tpc = p.tiles_per_combo;
-  const uint64_t combo = t / tpc;
-  const uint64_t rem = t - combo * tpc;
-  uint32_t lo = 0, hi = p.n_members;
-  while (hi - lo > 1) {
-    const uint32_t mid = (lo + hi) >> 1;
-    if (p.tile_prefix[mid] <= rem) lo = mid; else hi = mid;
-  }
-  const uint32_t m = lo;
-  const uint64_t tile_in_seg = rem - p.tile_prefix[m];
-  const uint32_t rk = (uint32_t)(combo % p.n_ranks);
-  const uint64_t bc = combo / p.n_ranks;
-  const uint32_t cb = (uint32_t)(bc % p.blocks_per_blob);
-  const uint32_t blob = (uint32_t)(bc / p.blocks_per_blob);
-  const uint64_t blob_base = p.blob_ptrs[blob];
-  if (blob_base == 0) {
-    r.skip = true;
-    return r;
-  }
-  const uint64_t sbb = p.member_bytes[m];
-  const uint64_t seg_off = tile_in_seg * p.tile_bytes;
-  r.len = (sbb - seg_off) < p.tile_bytes ? (sbb - seg_off) : p.tile_bytes;
-  const int64_t block = p.block_ids[(uint64_t)blob * p.blocks_per_blob + cb];
-  r.member = reinterpret_cast<uint8_t *>(p.member_ptrs[(uint64_t)rk * p.n_members + m]) + (uint64_t)block * sbb + seg_off;
-  r.blob = reinterpret_cast<uint8_t *>(blob_base) + p.region_bases[m] + (uint64_t)cb * sbb * p.n_ranks +
-           (uint64_t)rk * sbb + seg_off;
-  r.skip = false;
-  return r;
-}
 
 __device__ __forceinline__ bool tma_ok(const TileRef &r) {
   return ((reinterpret_cast<uint64_t>(r.member) | reinterpret_cast<uint64_t>(r.blob) | r.len) & 15u) == 0;
@@ -245,7 +220,7 @@ struct TileCursor {
     }
     const uint64_t seg_off = tile_in_seg * p->tile_bytes;
     r.len = (sbb - seg_off) < p->tile_bytes ? (sbb - seg_off) : p->tile_bytes;
-    r.member = reinterpret_cast<uint8_t *>(p->member_ptrs[(uint64_t)rk * p->n_members + m]) + (uint64_t)block * sbb +
+    r.member = reinterpret_cast<uint8_t *>(p->member_ptrs[member_index(*p, blob, rk, m)]) + (uint64_t)block * sbb +
                seg_off;
     r.blob = reinterpret_cast<uint8_t *>(blob_base) + p->region_bases[m] + (uint64_t)cb * sbb * p->n_ranks +
              (uint64_t)rk * sbb + seg_off;

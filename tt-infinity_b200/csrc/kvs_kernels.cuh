@@ -52,7 +52,8 @@ struct LookupOut {
 
 // Parameters of one chunk_copy launch. All arrays are device-accessible.
 struct ChunkCopyParams {
-  const uint64_t *member_ptrs;   // [n_ranks * n_members]
+  const uint64_t *member_ptrs;   // [n_sets * n_ranks * n_members]
+  const uint32_t *blob_sets;     // optional [n_blobs]: member set of each blob (nullptr: set 0)
   const uint64_t *member_bytes;  // [n_members] bytes of one block of the member
   const uint64_t *region_bases;  // [n_members] member region offset inside a blob
   const uint64_t *tile_prefix;   // [n_members + 1] tiles per member, prefix summed

@@ -13,6 +13,7 @@
 //     write-through stream, ordered after the gather by an event; the pending-host FIFO entry
 //     becomes committed at the next commit barrier (or earlier when allocation pressure forces
 //     it), exactly in issue order.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -200,6 +201,10 @@ struct kvs_server {
   kvs_move_profile mprof{};
   bool ready = false;
   bool quarantined = false;
+  // remote puts (kvs_grant_puts): the newest `unlanded` FIFO entries wait for kvs_puts_landed;
+  // grant_blocked: the last prepare asked for a commit of a value that had not landed
+  uint32_t unlanded = 0;
+  bool grant_blocked = false;
 
   uint64_t slab_base() const { return reinterpret_cast<uint64_t>(slab); }
 
@@ -286,6 +291,8 @@ struct kvs_server {
   // Commit the FIFO head, waiting for its device->host copy.
   int commit_one() {
     auto &head = dir->fifo_head();
+    if (head.wt_batch < 0)
+      return set_err(KVS_E_INVAL, "shard %u: a granted remote put has not landed yet (kvs_puts_landed)", cfg.shard_id);
     cudaEvent_t ev = event_for_batch((uint64_t)head.wt_batch);
     const uint64_t t0 = now_ns();
     if (ev) CUDA_TRY(cudaEventSynchronize(ev));
@@ -309,6 +316,9 @@ struct kvs_server {
   // COMMIT_BARRIER: every issued put becomes host-committed, in issue order.
   int commit_all() {
     if (dir->fifo_empty()) return KVS_OK;
+    if (unlanded)
+      return set_err(KVS_E_INVAL, "shard %u: %u granted remote puts have not landed yet (kvs_puts_landed)",
+                     cfg.shard_id, unlanded);
     cudaEvent_t last = event_for_batch((uint64_t)dir->fifo_back().wt_batch);
     if (last) CUDA_TRY(cudaEventSynchronize(last));
     while (!dir->fifo_empty()) TRY(commit_one());
@@ -1564,16 +1574,21 @@ static int launch_lookups(kvs_client *c, const ShardOrder &o, const uint8_t *d_k
   return KVS_OK;
 }
 
-int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const uint64_t *keys,
-                   const int64_t *block_ids, uint8_t *found, void *stream) {
-  TRY(check_client(c));
-  if (!found) return set_err(KVS_E_INVAL, "get_blocks: found is null");
-  BlockFormat fmt;
-  TRY(block_format(layout, &fmt));
-  TRY(check_blocks(layout, n, keys, block_ids, "get_blocks"));
-  std::lock_guard<std::mutex> lk(c->mu);
-  DeviceGuard g(c->device);
-  TRY(validate_layout_ptrs(c, layout, "get_blocks"));
+// Destination side of a block get: the value format, the member block sizes, and one or more
+// member sets (one per requesting paged pool; the owner of a shard serving several processes
+// scatters into each requester's pool over NVLink in one launch).
+struct GetTarget {
+  const BlockFormat *fmt;
+  uint32_t n_members;
+  const uint64_t *member_bytes;  // [n_members]
+  uint32_t n_sets;
+  const uint64_t *member_ptrs;   // [n_sets * n_members]
+  const uint32_t *sets;          // [n] member set of each key, or nullptr (set 0)
+};
+
+static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const uint64_t *keys,
+                           const int64_t *block_ids, uint8_t *found, void *stream) {
+  const BlockFormat &fmt = *t.fmt;
   const size_t ns = c->shards.size();
   std::vector<uint8_t> inv(ns, 0);
   std::vector<uint32_t> si(n);
@@ -1585,9 +1600,10 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
   ShardLocks locks(involved_servers(c, inv));
   TRY(quarantine_on_error(c, commit_barrier(c, inv)));  // GET preserves host-commit ordering first
   TRY(begin_op(c, stream));
+  const uint64_t ptr_bytes = 8ull * t.n_sets * t.n_members;
   // ---- pass 1: replica update, device lookup, scatter of device hits
   Staging &st = c->stage;
-  size_t need = 4096 + 64ull * n + 40ull * layout->n_members;
+  size_t need = 4096 + 68ull * n + ptr_bytes + 32ull * t.n_members;
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) need += mutation_upper_bound(c->shards[i]);
   TRY(st.begin(need, c->stream));
@@ -1600,10 +1616,15 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     st.h<uint64_t>(keys_off)[j] = keys[ord.perm[j]];
     st.h<int64_t>(ids_off)[j] = block_ids[ord.perm[j]];
   }
-  const size_t mp_off = st.push(layout->member_ptrs, 8ull * layout->n_members);
-  const size_t mb_off = st.push(layout->member_block_bytes, 8ull * layout->n_members);
-  const size_t rb_off = st.push(fmt.region_bases.data(), 8ull * layout->n_members);
-  const size_t tp_off = st.push(fmt.tile_prefix.data(), 8ull * (layout->n_members + 1));
+  size_t sets_off = 0;
+  if (t.sets) {
+    sets_off = st.take(4ull * n);
+    for (uint32_t j = 0; j < n; ++j) st.h<uint32_t>(sets_off)[j] = t.sets[ord.perm[j]];
+  }
+  const size_t mp_off = st.push(t.member_ptrs, ptr_bytes);
+  const size_t mb_off = st.push(t.member_bytes, 8ull * t.n_members);
+  const size_t rb_off = st.push(fmt.region_bases.data(), 8ull * t.n_members);
+  const size_t tp_off = st.push(fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
   const size_t upload_bytes = st.used;
   const size_t out_off = st.take(sizeof(kvs::LookupOut) * n);
   const size_t blob_off = st.take(8ull * n);
@@ -1616,6 +1637,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
                                             st.d<uint64_t>(blob_off), fmt.value_len)));
   kvs::ChunkCopyParams p{};
   p.member_ptrs = st.d<uint64_t>(mp_off);
+  p.blob_sets = t.sets ? st.d<uint32_t>(sets_off) : nullptr;
   p.member_bytes = st.d<uint64_t>(mb_off);
   p.region_bases = st.d<uint64_t>(rb_off);
   p.tile_prefix = st.d<uint64_t>(tp_off);
@@ -1624,13 +1646,13 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
   p.n_blobs = n;
   p.blocks_per_blob = 1;
   p.n_ranks = 1;
-  p.n_members = layout->n_members;
+  p.n_members = t.n_members;
   p.tile_bytes = kTileBytes;
   p.tiles_per_combo = fmt.tile_prefix.back();
   p.total_tiles = (uint64_t)n * p.tiles_per_combo;
   p.to_blob = 0;
   uint64_t payload_per_block = 0;
-  for (uint32_t m = 0; m < layout->n_members; ++m) payload_per_block += layout->member_block_bytes[m];
+  for (uint32_t m = 0; m < t.n_members; ++m) payload_per_block += t.member_bytes[m];
   cudaEvent_t t0 = nullptr;
   c->time_begin(&t0);
   CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
@@ -1669,9 +1691,12 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     uint64_t len;
     bool scatter;  // pass 1 did not deliver it (host-tier hit)
     uint64_t host_dev;  // device alias of the host copy
+    uint64_t slab_src;  // pass 2 scatters from this slab block (0: from the host copy)
+    bool moved;  // a host-tier serve (counted as a move to the device side)
   };
   std::vector<Late> late;
-  std::map<std::pair<uint32_t, uint32_t>, size_t> admitted;  // (shard, slot) -> index in late
+  // (shard, slot) -> late entries that read the slot's slab block in pass 2
+  std::multimap<std::pair<uint32_t, uint32_t>, size_t> reads;
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) c->shards[i]->dir->take_evicted();
   for (uint32_t i = 0; i < n; ++i) {
@@ -1681,25 +1706,35 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     uint64_t off = 0;
     const auto action = s->dir->get_hit(host_slot[i], &off);
     found[i] = 1;
-    // an admission earlier in this batch whose block was just evicted again: serve that one
-    // from its host copy instead of the (reused) block
+    // a block admitted earlier in this batch and just evicted again: the gets that were to read
+    // it read the host copy instead, and its admission copy is dropped
     for (uint32_t ev : s->dir->take_evicted()) {
-      auto it = admitted.find({si[i], ev});
-      if (it != admitted.end()) late[it->second].admit_dst = 0;
+      auto range = reads.equal_range({si[i], ev});
+      for (auto it = range.first; it != range.second; ++it) {
+        late[it->second].admit_dst = 0;
+        late[it->second].slab_src = 0;
+      }
+      reads.erase(range.first, range.second);
     }
-    if (action == Directory::GetAction::kDevice) continue;
     const HostBacking &hb = s->dir->backing(host_slot[i]);
     Late L{i, si[i], host_slot[i], 0, s->host_ptr(hb), s->dir->entry(host_slot[i]).total_len,
-           res[i].status == kvs::kHitHost, s->device_alias(hb)};
-    if (action == Directory::GetAction::kAdmit) {
-      L.admit_dst = s->slab_base() + off;
-      admitted[{si[i], host_slot[i]}] = late.size();
+           res[i].status == kvs::kHitHost, s->device_alias(hb), 0, true};
+    if (action == Directory::GetAction::kDevice) {
+      if (!L.scatter) continue;  // delivered by pass 1
+      // pass 1 saw the host tier, and an earlier get of this batch has admitted the value since:
+      // read the block that admission fills
+      L.slab_src = s->slab_base() + s->dir->entry(host_slot[i]).value_off;
+      L.moved = false;
+      reads.insert({{si[i], host_slot[i]}, late.size()});
+    } else if (action == Directory::GetAction::kAdmit) {
+      L.admit_dst = L.slab_src = s->slab_base() + off;
+      reads.insert({{si[i], host_slot[i]}, late.size()});
     }
     late.push_back(L);
   }
   if (!late.empty()) {
     // ---- pass 2: replica update, admissions (host -> slab), scatter of host-tier hits
-    size_t need2 = 4096 + 32ull * late.size() + 40ull * layout->n_members;
+    size_t need2 = 4096 + 36ull * late.size() + ptr_bytes + 32ull * t.n_members;
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) need2 += mutation_upper_bound(c->shards[i]);
     TRY(st.begin(need2, c->stream));
@@ -1710,18 +1745,21 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     for (auto &L : late) nscatter += L.scatter;
     const size_t blobs2 = st.take(8 * std::max<size_t>(nscatter, 1));
     const size_t ids2 = st.take(8 * std::max<size_t>(nscatter, 1));
+    const size_t sets2 = st.take(4 * std::max<size_t>(nscatter, 1));
     size_t k = 0;
     for (auto &L : late)
       if (L.scatter) {
-        // admitted values are scattered from their new slab block, others from host memory
-        st.h<uint64_t>(blobs2)[k] = L.admit_dst ? L.admit_dst : L.host_dev;
+        // values in the slab (admitted in this batch) are scattered from their block, others
+        // from host memory
+        st.h<uint64_t>(blobs2)[k] = L.slab_src ? L.slab_src : L.host_dev;
         st.h<int64_t>(ids2)[k] = block_ids[L.i];
+        st.h<uint32_t>(sets2)[k] = t.sets ? t.sets[L.i] : 0;
         ++k;
       }
-    const size_t mp2 = st.push(layout->member_ptrs, 8ull * layout->n_members);
-    const size_t mb2 = st.push(layout->member_block_bytes, 8ull * layout->n_members);
-    const size_t rb2 = st.push(fmt.region_bases.data(), 8ull * layout->n_members);
-    const size_t tp2 = st.push(fmt.tile_prefix.data(), 8ull * (layout->n_members + 1));
+    const size_t mp2 = st.push(t.member_ptrs, ptr_bytes);
+    const size_t mb2 = st.push(t.member_bytes, 8ull * t.n_members);
+    const size_t rb2 = st.push(fmt.region_bases.data(), 8ull * t.n_members);
+    const size_t tp2 = st.push(fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
     TRY(st.upload(c->stream, st.used));
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) TRY(chain_wait(c, c->shards[i]));
@@ -1734,6 +1772,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     if (nscatter) {
       kvs::ChunkCopyParams q = p;
       q.member_ptrs = st.d<uint64_t>(mp2);
+      q.blob_sets = t.sets ? st.d<uint32_t>(sets2) : nullptr;
       q.member_bytes = st.d<uint64_t>(mb2);
       q.region_bases = st.d<uint64_t>(rb2);
       q.tile_prefix = st.d<uint64_t>(tp2);
@@ -1747,6 +1786,7 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
       if (inv[i]) TRY(chain_record(c, i));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     for (auto &L : late) {
+      if (!L.moved) continue;
       kvs_server *s = c->shards[L.shard];
       s->mprof.to_device_count++;
       s->moves_completed.fetch_add(1, std::memory_order_relaxed);
@@ -1757,6 +1797,20 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
     return set_err(KVS_E_FORMAT, "get_blocks: stored value for key %d has length %u, the block layout needs %llu",
                    format_error, res[format_error].value_len, (unsigned long long)fmt.value_len);
   return KVS_OK;
+}
+
+int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const uint64_t *keys,
+                   const int64_t *block_ids, uint8_t *found, void *stream) {
+  TRY(check_client(c));
+  if (!found) return set_err(KVS_E_INVAL, "get_blocks: found is null");
+  BlockFormat fmt;
+  TRY(block_format(layout, &fmt));
+  TRY(check_blocks(layout, n, keys, block_ids, "get_blocks"));
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(validate_layout_ptrs(c, layout, "get_blocks"));
+  GetTarget t{&fmt, layout->n_members, layout->member_block_bytes, 1, layout->member_ptrs, nullptr};
+  return get_blocks_impl(c, t, n, keys, block_ids, found, stream);
 }
 
 int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found) {
@@ -1805,6 +1859,359 @@ int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *f
       return set_err(KVS_E_CUDA, "exists_batch: device index replica disagrees with the catalog for key %u", i);
     }
   }
+  return KVS_OK;
+}
+
+// ---------------------------------------------------------------------------- shards in other processes
+
+namespace {
+
+// cuMemGetAddressRange through the runtime's driver entry point (no link against libcuda).
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr *base, size_t *size, CUdeviceptr ptr);
+
+GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return (GetAddressRangeFn) nullptr;
+    }
+    return reinterpret_cast<GetAddressRangeFn>(f);
+  }();
+  return fn;
+}
+
+// Member pointers of the requesters' pools that were checked to be device memory.
+std::mutex g_checked_mu;
+std::vector<uint64_t> g_checked_members;
+
+int check_member_sets(const kvs_block_layout *layouts, uint32_t n_sets, const char *op) {
+  std::lock_guard<std::mutex> lk(g_checked_mu);
+  for (uint32_t s = 0; s < n_sets; ++s)
+    for (uint32_t m = 0; m < layouts[s].n_members; ++m) {
+      const uint64_t ptr = layouts[s].member_ptrs[m];
+      if (std::find(g_checked_members.begin(), g_checked_members.end(), ptr) != g_checked_members.end()) continue;
+      cudaPointerAttributes a{};
+      if (cudaPointerGetAttributes(&a, reinterpret_cast<const void *>(ptr)) != cudaSuccess ||
+          a.type != cudaMemoryTypeDevice) {
+        cudaGetLastError();
+        return set_err(KVS_E_INVAL, "%s: member %u of pool %u must be device memory (this GPU's or a peer's)", op, m,
+                       s);
+      }
+      g_checked_members.push_back(ptr);
+    }
+  return KVS_OK;
+}
+
+int owner_shard(kvs_client *c, const char *op, kvs_server **s) {
+  TRY(check_client(c));
+  if (c->shards.size() != 1)
+    return set_err(KVS_E_INVAL, "%s: the owner's client must have exactly one shard (has %zu)", op, c->shards.size());
+  *s = c->shards[0];
+  return KVS_OK;
+}
+
+// One copy launch between whole values at `addrs` and rows of `value_len` bytes (raw values, no
+// header). to_rows: addrs[i] -> rows[i].
+int copy_values_launch(kvs_client *c, uint64_t rows, uint64_t value_len, uint32_t n, const uint64_t *addrs,
+                       int to_rows) {
+  Staging &st = c->stage;
+  TRY(st.begin(4096 + 16ull * n, c->stream));
+  const size_t blobs = st.push(addrs, 8ull * n);
+  const size_t ids = st.take(8ull * n);
+  for (uint32_t i = 0; i < n; ++i) st.h<int64_t>(ids)[i] = i;
+  const uint64_t meta[5] = {rows, value_len, 0, 0, (value_len + kTileBytes - 1) / kTileBytes};
+  const size_t mo = st.push(meta, sizeof meta);
+  TRY(st.upload(c->stream, st.used));
+  kvs::ChunkCopyParams p{};
+  p.member_ptrs = st.d<uint64_t>(mo);
+  p.member_bytes = st.d<uint64_t>(mo + 8);
+  p.region_bases = st.d<uint64_t>(mo + 16);
+  p.tile_prefix = st.d<uint64_t>(mo + 24);
+  p.block_ids = st.d<int64_t>(ids);
+  p.blob_ptrs = st.d<uint64_t>(blobs);
+  p.n_blobs = n;
+  p.blocks_per_blob = 1;
+  p.n_ranks = 1;
+  p.n_members = 1;
+  p.tile_bytes = kTileBytes;
+  p.tiles_per_combo = meta[4];
+  p.total_tiles = (uint64_t)n * p.tiles_per_combo;
+  p.to_blob = to_rows ? 0 : 1;
+  CUDA_TRY(launch_copy(p, c->stream, false, c->timeout_flag));
+  return KVS_OK;
+}
+
+}  // namespace
+
+int kvs_ipc_export(const void *ptr, kvs_ipc_handle *handle, uint64_t *offset) {
+  if (!ptr || !handle || !offset) return set_err(KVS_E_INVAL, "ipc_export: null argument");
+  static_assert(sizeof(kvs_ipc_handle) == sizeof(cudaIpcMemHandle_t), "kvs_ipc_handle is a cudaIpcMemHandle_t");
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return set_err(KVS_E_INVAL, "ipc_export: pointer is not device memory");
+  }
+  DeviceGuard g(a.device);
+  GetAddressRangeFn range = address_range_fn();
+  if (!range) return set_err(KVS_E_CUDA, "ipc_export: cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return set_err(KVS_E_INVAL, "ipc_export: no device allocation contains the pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(KVS_E_INVAL, "ipc_export: %s (the allocation must come from cudaMalloc)", cudaGetErrorString(e));
+  }
+  std::memcpy(handle->bytes, &h, sizeof h);
+  *offset = reinterpret_cast<uint64_t>(ptr) - (uint64_t)base;
+  return KVS_OK;
+}
+
+int kvs_ipc_open(int32_t device, const kvs_ipc_handle *handle, void **base) {
+  if (!handle || !base) return set_err(KVS_E_INVAL, "ipc_open: null argument");
+  *base = nullptr;
+  DeviceGuard g(device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof h);
+  cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(KVS_E_CUDA, "ipc_open: %s", cudaGetErrorString(e));
+  }
+  return KVS_OK;
+}
+
+int kvs_ipc_close(int32_t device, void *base) {
+  if (!base) return KVS_OK;
+  DeviceGuard g(device);
+  {
+    // pointers inside the closed mapping are no longer known device memory
+    std::lock_guard<std::mutex> lk(g_checked_mu);
+    g_checked_members.clear();
+  }
+  CUDA_TRY(cudaIpcCloseMemHandle(base));
+  return KVS_OK;
+}
+
+int kvs_server_slab(kvs_server *s, void **base, uint64_t *bytes) {
+  if (!s || !base || !bytes) return set_err(KVS_E_INVAL, "server_slab: null argument");
+  *base = s->slab;
+  *bytes = s->cfg.heap_bytes;
+  return KVS_OK;
+}
+
+int kvs_serve_gets(kvs_client *c, uint32_t n_sets, const kvs_block_layout *layouts, uint32_t n, const uint32_t *sets,
+                   const int64_t *block_ids, const uint64_t *keys, uint8_t *found, void *stream) {
+  kvs_server *s = nullptr;
+  TRY(owner_shard(c, "serve_gets", &s));
+  if (n_sets == 0 || !layouts) return set_err(KVS_E_INVAL, "serve_gets: at least one pool layout is required");
+  BlockFormat fmt;
+  TRY(block_format(&layouts[0], &fmt));
+  for (uint32_t k = 1; k < n_sets; ++k) {
+    const kvs_block_layout &L = layouts[k];
+    BlockFormat fk;
+    TRY(block_format(&L, &fk));  // validates pointers and sizes of every layout
+    bool same = L.n_members == layouts[0].n_members && L.members_per_layer == layouts[0].members_per_layer;
+    for (uint32_t m = 0; same && m < L.n_members; ++m) same = L.member_block_bytes[m] == layouts[0].member_block_bytes[m];
+    if (!same) return set_err(KVS_E_INVAL, "serve_gets: pool %u has other member sizes than pool 0", k);
+  }
+  if (n && (!sets || !block_ids || !keys || !found)) return set_err(KVS_E_INVAL, "serve_gets: null argument");
+  for (uint32_t i = 0; i < n; ++i) {
+    if (sets[i] >= n_sets) return set_err(KVS_E_INVAL, "serve_gets: pool %u of key %u out of range", sets[i], i);
+    if (block_ids[i] < 0 || (uint64_t)block_ids[i] >= layouts[sets[i]].n_pool_blocks)
+      return set_err(KVS_E_INVAL, "serve_gets: block id %lld at %u is outside the %llu-block pool",
+                     (long long)block_ids[i], i, (unsigned long long)layouts[sets[i]].n_pool_blocks);
+  }
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  if (n == 0) {
+    std::lock_guard<std::mutex> sl(s->mu);
+    return quarantine_on_error(c, s->commit_all());
+  }
+  TRY(check_member_sets(layouts, n_sets, "serve_gets"));
+  const uint32_t nm = layouts[0].n_members;
+  std::vector<uint64_t> ptrs((size_t)n_sets * nm);
+  for (uint32_t k = 0; k < n_sets; ++k)
+    std::memcpy(ptrs.data() + (size_t)k * nm, layouts[k].member_ptrs, 8ull * nm);
+  GetTarget t{&fmt, nm, layouts[0].member_block_bytes, n_sets, ptrs.data(), sets};
+  return get_blocks_impl(c, t, n, keys, block_ids, found, stream);
+}
+
+int kvs_serve_gets_packed(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *keys,
+                          uint8_t *found, void *stream) {
+  kvs_server *s = nullptr;
+  TRY(owner_shard(c, "serve_gets_packed", &s));
+  if (value_len == 0 || value_len % 4) return set_err(KVS_E_INVAL, "serve_gets_packed: value_len must be a nonzero multiple of 4");
+  if (n && (!rows || !keys || !found)) return set_err(KVS_E_INVAL, "serve_gets_packed: null argument");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  if (n == 0) {
+    std::lock_guard<std::mutex> sl(s->mu);
+    return quarantine_on_error(c, s->commit_all());
+  }
+  TRY(check_device_ptr(c, rows, "serve_gets_packed", "rows"));
+  BlockFormat fmt;  // a whole value is one member region at offset 0
+  fmt.region_bases = {0};
+  fmt.tile_prefix = {0, (value_len + kTileBytes - 1) / kTileBytes};
+  fmt.value_len = value_len;
+  const uint64_t member_bytes = value_len, member_ptr = reinterpret_cast<uint64_t>(rows);
+  std::vector<int64_t> ids(n);
+  for (uint32_t i = 0; i < n; ++i) ids[i] = i;
+  GetTarget t{&fmt, 1, &member_bytes, 1, &member_ptr, nullptr};
+  return get_blocks_impl(c, t, n, keys, ids.data(), found, stream);
+}
+
+int kvs_grant_puts(kvs_client *c, uint32_t n, const uint64_t *keys, uint64_t value_len, uint64_t *slab_offsets,
+                   uint32_t *n_granted) {
+  kvs_server *s = nullptr;
+  TRY(owner_shard(c, "grant_puts", &s));
+  if (!n_granted) return set_err(KVS_E_INVAL, "grant_puts: n_granted is null");
+  *n_granted = 0;
+  if (n && (!keys || !slab_offsets)) return set_err(KVS_E_INVAL, "grant_puts: null argument");
+  if (value_len == 0 || value_len > s->cfg.max_value_bytes)
+    return set_err(KVS_E_INVAL, "grant_puts: value of %llu B is outside (0, max_value_bytes %llu]",
+                   (unsigned long long)value_len, (unsigned long long)s->cfg.max_value_bytes);
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  std::lock_guard<std::mutex> sl(s->mu);
+  if (s->grant_blocked) {
+    // the prepare that stopped the last grant asked for this commit; its value has landed since
+    TRY(quarantine_on_error(c, s->commit_one()));
+    s->retire_batches();
+    s->release_dropped();
+    s->grant_blocked = false;
+  }
+  uint32_t i = 0;
+  for (; i < n; ++i) {
+    bool granted = false;
+    for (;;) {
+      kvs::Grant gr;
+      const kvs::Prepare r = s->dir->prepare_put((const uint8_t *)&keys[i], 8, value_len, &gr);
+      if (r == kvs::Prepare::kGranted) {
+        slab_offsets[i] = gr.value_off;
+        s->unlanded++;
+        granted = true;
+        break;
+      }
+      if (r == kvs::Prepare::kNoSpace) {
+        *n_granted = i;
+        return set_err(KVS_E_NOSPACE, "grant_puts: no device-cache space for a %llu B value",
+                       (unsigned long long)value_len);
+      }
+      if (s->dir->fifo_head().wt_batch < 0) {
+        s->grant_blocked = true;  // force_put_host_commit of a value still in flight: next round
+        break;
+      }
+      TRY(quarantine_on_error(c, s->commit_one()));  // force_put_host_commit, then retry the prepare
+      s->retire_batches();
+      s->release_dropped();
+    }
+    if (!granted) break;
+  }
+  *n_granted = i;
+  return KVS_OK;
+}
+
+int kvs_puts_landed(kvs_client *c, void *stream) {
+  kvs_server *s = nullptr;
+  TRY(owner_shard(c, "puts_landed", &s));
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  std::lock_guard<std::mutex> sl(s->mu);
+  if (!s->unlanded) return KVS_OK;
+  auto &fifo = s->dir->fifo();
+  if (fifo.size() < s->unlanded) {
+    c->quarantined = true;
+    return set_err(KVS_E_CUDA, "puts_landed: the pending FIFO lost granted entries");
+  }
+  CUDA_TRY(cudaEventRecord(c->landed_evt, stream ? (cudaStream_t)stream : c->stream));
+  CUDA_TRY(cudaStreamWaitEvent(s->wt_stream, c->landed_evt, 0));
+  uint64_t batch_id = 0;
+  cudaEvent_t ev = nullptr;
+  TRY(s->new_batch(&batch_id, &ev));
+  for (size_t k = fifo.size() - s->unlanded; k < fifo.size(); ++k) {
+    kvs::PendingPut &pp = fifo[k];
+    const kvs::Entry &e = s->dir->entry(pp.slot);
+    TRY(s->reserve_backing(e.total_len, &pp.backing));
+    pp.wt_batch = (int)batch_id;
+    CUDA_TRY(cudaMemcpyAsync(s->host_ptr(pp.backing), s->slab + e.value_off, e.total_len, cudaMemcpyDeviceToHost,
+                             s->wt_stream));
+  }
+  CUDA_TRY(cudaEventRecord(ev, s->wt_stream));
+  s->unlanded = 0;
+  return KVS_OK;
+}
+
+int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const int64_t *block_ids,
+                    const uint64_t *blob_addrs, int to_blob, void *stream) {
+  TRY(check_client(c));
+  BlockFormat fmt;
+  TRY(block_format(layout, &fmt));
+  if (n == 0) return KVS_OK;
+  if (!block_ids || !blob_addrs) return set_err(KVS_E_INVAL, "copy_blocks: null argument");
+  for (uint32_t i = 0; i < n; ++i) {
+    if (block_ids[i] < 0 || (uint64_t)block_ids[i] >= layout->n_pool_blocks)
+      return set_err(KVS_E_INVAL, "copy_blocks: block id %lld at %u is outside the %llu-block pool",
+                     (long long)block_ids[i], i, (unsigned long long)layout->n_pool_blocks);
+    if (blob_addrs[i] & 15u) return set_err(KVS_E_INVAL, "copy_blocks: value address %u is not 16-byte aligned", i);
+  }
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(validate_layout_ptrs(c, layout, "copy_blocks"));
+  TRY(begin_op(c, stream));
+  Staging &st = c->stage;
+  TRY(st.begin(4096 + 16ull * n + 40ull * layout->n_members + 4ull * fmt.header.size(), c->stream));
+  const size_t blobs = st.push(blob_addrs, 8ull * n);
+  const size_t ids = st.push(block_ids, 8ull * n);
+  const size_t mp = st.push(layout->member_ptrs, 8ull * layout->n_members);
+  const size_t mb = st.push(layout->member_block_bytes, 8ull * layout->n_members);
+  const size_t rb = st.push(fmt.region_bases.data(), 8ull * layout->n_members);
+  const size_t tp = st.push(fmt.tile_prefix.data(), 8ull * (layout->n_members + 1));
+  const size_t hw = st.push(fmt.header.data(), 4ull * fmt.header.size());
+  TRY(st.upload(c->stream, st.used));
+  kvs::ChunkCopyParams p{};
+  p.member_ptrs = st.d<uint64_t>(mp);
+  p.member_bytes = st.d<uint64_t>(mb);
+  p.region_bases = st.d<uint64_t>(rb);
+  p.tile_prefix = st.d<uint64_t>(tp);
+  p.block_ids = st.d<int64_t>(ids);
+  p.blob_ptrs = st.d<uint64_t>(blobs);
+  p.header_words = st.d<uint32_t>(hw);
+  p.n_header_words = to_blob ? (uint32_t)fmt.header.size() : 0;
+  p.n_blobs = n;
+  p.blocks_per_blob = 1;
+  p.n_ranks = 1;
+  p.n_members = layout->n_members;
+  p.tile_bytes = kTileBytes;
+  p.tiles_per_combo = fmt.tile_prefix.back();
+  p.total_tiles = (uint64_t)n * p.tiles_per_combo;
+  p.to_blob = to_blob ? 1 : 0;
+  uint64_t payload = 0;
+  for (uint32_t m = 0; m < layout->n_members; ++m) payload += layout->member_block_bytes[m];
+  cudaEvent_t t0 = nullptr;
+  c->time_begin(&t0);
+  CUDA_TRY(launch_copy(p, c->stream, false, c->timeout_flag));
+  c->time_end(t0, to_blob ? 0 : 1, (uint64_t)n * payload);
+  TRY(end_op(c, stream));
+  return KVS_OK;
+}
+
+int kvs_copy_values(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *addrs, int to_rows,
+                    void *stream) {
+  TRY(check_client(c));
+  if (n == 0) return KVS_OK;
+  if (!rows || !addrs || value_len == 0) return set_err(KVS_E_INVAL, "copy_values: null argument or empty value");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  TRY(check_device_ptr(c, rows, "copy_values", "rows"));
+  TRY(begin_op(c, stream));
+  TRY(copy_values_launch(c, reinterpret_cast<uint64_t>(rows), value_len, n, addrs, to_rows));
+  TRY(end_op(c, stream));
   return KVS_OK;
 }
 

@@ -139,6 +139,10 @@ Stats = _u64_struct(
     [("epoch", C.c_uint32), ("issued", C.c_uint32), ("committed", C.c_uint32), ("kernel_launches", C.c_uint64)],
 )
 
+class IpcHandle(C.Structure):
+    _fields_ = [("bytes", C.c_uint8 * 64)]
+
+
 class KernelTiming(C.Structure):
     _fields_ = [("launches", C.c_uint64), ("bytes", C.c_uint64), ("total_ms", C.c_double)]
 
@@ -186,6 +190,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvs_put_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, _u64p, _i64p, C.c_int, P]),
     "kvs_get_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, _u64p, _i64p, _u8p, P]),
     "kvs_exists_batch": (C.c_int, [P, C.c_uint32, _u64p, _u8p]),
+    "kvs_ipc_export": (C.c_int, [P, C.POINTER(IpcHandle), _u64p]),
+    "kvs_ipc_open": (C.c_int, [C.c_int32, C.POINTER(IpcHandle), C.POINTER(P)]),
+    "kvs_ipc_close": (C.c_int, [C.c_int32, P]),
+    "kvs_server_slab": (C.c_int, [P, C.POINTER(P), _u64p]),
+    "kvs_serve_gets": (C.c_int, [P, C.c_uint32, C.POINTER(BlockLayout), C.c_uint32, _u32p, _i64p, _u64p, _u8p, P]),
+    "kvs_serve_gets_packed": (C.c_int, [P, P, C.c_uint64, C.c_uint32, _u64p, _u8p, P]),
+    "kvs_grant_puts": (C.c_int, [P, C.c_uint32, _u64p, C.c_uint64, _u64p, _u32p]),
+    "kvs_puts_landed": (C.c_int, [P, P]),
+    "kvs_copy_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, _i64p, _u64p, C.c_int, P]),
+    "kvs_copy_values": (C.c_int, [P, P, C.c_uint64, C.c_uint32, _u64p, C.c_int, P]),
     "kvs_client_set_timing": (C.c_int, [P, C.c_int]),
     "kvs_client_timing": (C.c_int, [P, C.POINTER(KernelTiming), C.POINTER(KernelTiming)]),
     "kvs_gather_chunk": (
