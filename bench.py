@@ -10,9 +10,15 @@ rate. Values are seeded N(0,1) bf16; block tables are random permutations of the
 64-bit chained prefix-block hashes, fresh for every step. The metric is payload GB/s of put + get
 (2 x 2 GiB per step).
 
-N > 1 (torchrun, one rank per GPU): every rank runs the same workload against its own shard on its
-own GPU (weak scaling, no data-path collective); time is the max over ranks and `value` is the
-bytes all ranks moved divided by it.
+N > 1 (torchrun, one rank per GPU): one store hash-sharded over all GPUs (kvcache_manager.sharded).
+Every rank gets back the 128 blocks it put in the previous step and puts a fresh prompt; blocks
+owned by other GPUs cross NVLink as P2P stores issued by the copy kernels (weak scaling: the
+per-rank work is fixed). Time is the max over ranks and `value` is the bytes all ranks moved
+divided by it. --parallelism independent gives each GPU its own store instead; --transport nccl
+moves packed values with NCCL send/recv.
+
+--mix (torchrun, N > 1): the hash-sharded 70/30 get/put mix of 256-block batches with the config-1
+KV shape and `--resident` blocks per GPU, timed with both transports on the same store.
 
 --impl reference times the reference's host-DRAM path restated in C (the oracle: run planner,
 memcpy gather/scatter, directory, host write-through) on the host cores with all threads.
@@ -64,6 +70,15 @@ def parse() -> argparse.Namespace:
                     help="32 sessions x 5 turns of prefix reuse with a slab of 25%% of the working set")
     ap.add_argument("--small", action="store_true",
                     help="profiling case: 16 layers, 512-block pool, 64 blocks per step (same kernels)")
+    ap.add_argument("--parallelism", choices=["sharded", "independent"], default="sharded",
+                    help="N > 1: one hash-sharded store over all GPUs (default) or an independent store per GPU")
+    ap.add_argument("--transport", choices=["p2p", "nccl"], default="p2p",
+                    help="sharded store: P2P stores over NVLink (default) or NCCL send/recv of packed values")
+    ap.add_argument("--mix", action="store_true",
+                    help="hash-sharded 70/30 get/put mix of 256-block batches, config-1 KV shape, both transports")
+    ap.add_argument("--resident", type=int, default=0,
+                    help="--mix: resident blocks per GPU (default: 1M / N, at most 16384: the pinned host "
+                         "tier mirrors every resident block)")
     args = ap.parse_args()
     if args.small:
         global LAYERS, POOL_BLOCKS, BATCH_BLOCKS, BLOCK_PAYLOAD, WORKLOAD
@@ -156,11 +171,11 @@ def ncu_traffic_per_launch(kernel: str):
 # ------------------------------------------------------------------ the GPU workload
 
 
-def build_pool(torch, device):
+def build_pool(torch, device, rank=0):
     """128 member tensors (K, V per layer) of (4096, 8, 64, 128) bf16 filled with seeded N(0,1)."""
     kv = []
     g = torch.Generator(device=device)
-    g.manual_seed(20261201)
+    g.manual_seed(20261201 + rank)
     for _ in range(LAYERS):
         pair = []
         for _ in range(2):
@@ -370,6 +385,336 @@ def run_ours(args, rank, local_rank, world):
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(seconds=12.0)
     return line
+
+
+# ------------------------------------------------------------------ hash-sharded store over N GPUs
+
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
+
+
+def _max_over_ranks(torch, dist, value, device):
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(torch, dist, value, device):
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+def _pcie_d2h_peak(torch, device):
+    pin = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    src_buf = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    best = 0.0
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        pin.copy_(src_buf, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        best = max(best, (1 << 30) / (e0.elapsed_time(e1) / 1e3) / GB)
+    return best
+
+
+def _nvlink_roofline(torch, dist, device, timing, counters0, counters1, payload):
+    """Per launch: the payload bytes that crossed NVLink / the launch's device time, for the client
+    put kernel (P2P stores into the owners' slabs) and the owner get kernel (P2P stores into the
+    requesters' pools); the dominant one by device time is the roofline kernel."""
+    g, s = timing["gather"], timing["scatter"]
+    out = {}
+    for name, t, key in (("put_push", g, "puts_remote"), ("get_push", s, "served_remote")):
+        remote = (counters1[key] - counters0[key]) * payload
+        ms = t["total_ms"]
+        launches = max(1, t["launches"])
+        out[name] = {"launches": t["launches"], "avg_ms": round(ms / launches, 4),
+                     "nvlink_bytes_per_launch": int(remote / launches),
+                     "achieved_nvlink_GBps": round(remote / max(ms / 1e3, 1e-12) / GB, 1),
+                     "hbm_GBps_2x_payload": round(2 * t["bytes"] / max(ms / 1e3, 1e-12) / GB, 1)}
+    dom = "put_push" if g["total_ms"] >= s["total_ms"] else "get_push"
+    # rank 0's view, max over ranks of launch time is what bounds the step
+    achieved = _sum_over_ranks(torch, dist, out[dom]["achieved_nvlink_GBps"], device) / dist.get_world_size()
+    return dom, out, achieved
+
+
+def run_sharded(args, rank, local_rank, world):
+    """The Qwen3-32B-shaped step through one store hash-sharded over all N GPUs: every rank gets
+    back the 128 blocks it put in the previous step and puts a fresh 8192-token prompt; (N-1)/N of
+    the blocks live on other GPUs and cross NVLink as P2P stores."""
+    import torch
+    import torch.distributed as dist
+
+    from kvcache_manager import PagedLayout, _native, codec, sharded
+
+    device = local_rank
+    torch.cuda.set_device(device)
+    kv = build_pool(torch, device, rank)
+    layout = PagedLayout.from_kv_caches(kv)
+    vlen = layout.value_bytes()
+    units = -(-vlen // UNIT_BYTES)
+    block_units = 1 << (units - 1).bit_length()
+    slab_values = 3 * BATCH_BLOCKS
+    max_keys = 4 * BATCH_BLOCKS
+    store = sharded.create(layout, max_batch=BATCH_BLOCKS, transport=args.transport, max_keys=max_keys,
+                           heap_bytes=slab_values * block_units * UNIT_BYTES,
+                           host_pool_bytes=(max_keys + 8) * units * UNIT_BYTES, max_value_bytes=64 << 20)
+    eng = store.engine
+    rng = np.random.default_rng(1000 + rank)
+    lib = _native.load()
+    prev = {"keys": np.zeros(0, np.uint64)}
+
+    def one_step(step):
+        perm = rng.permutation(POOL_BLOCKS)
+        keys = np.array(codec.chained_block_hashes(step * 7919 + rank * 104729 + 1, BATCH_BLOCKS), np.uint64)
+        src, dst = perm[:BATCH_BLOCKS].astype(np.int64), perm[BATCH_BLOCKS:2 * BATCH_BLOCKS].astype(np.int64)
+        gk = prev["keys"]
+        gd = dst[:gk.size]
+        found = store.step(gk, gd, keys, src)
+        if not found.all():
+            raise RuntimeError(f"step {step}: device-tier get missed {int((~found).sum())} blocks")
+        prev["keys"], prev["src"] = keys, src
+        return gd
+
+    def checksums(blocks):
+        idx = torch.as_tensor(blocks, device=device)
+        return [int(t[idx].view(torch.int16).to(torch.int64).sum()) for layer in (0, LAYERS // 2, LAYERS - 1)
+                for t in kv[layer]]
+
+    # correctness gate: blocks restored from the (mostly remote) shards equal their sources
+    one_step(0)
+    torch.cuda.synchronize()
+    want = checksums(prev["src"])
+    got_blocks = one_step(1)
+    torch.cuda.synchronize()
+    if checksums(got_blocks) != want:
+        raise RuntimeError(f"rank {rank}: restored blocks differ from the source blocks")
+    for w in range(args.warmup):
+        one_step(2 + w)
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    sampler = ClockSampler([device]) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    eng.client.kernel_timing()
+    eng.client.set_kernel_timing(True)
+    c0 = dict(store.counters)
+    launches0 = lib.kvs_kernel_launch_count()
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    start.record(stream)
+    for k in range(args.steps):
+        one_step(1000 + k)
+    store.flush()  # this shard's puts of the timed region are host-committed inside it
+    end.record(stream)
+    torch.cuda.synchronize()
+    launches = lib.kvs_kernel_launch_count() - launches0
+    elapsed_ms = _max_over_ranks(torch, dist, start.elapsed_time(end), device)
+    timing = eng.client.kernel_timing()
+    eng.client.set_kernel_timing(False)
+    c1 = dict(store.counters)
+    clocks = sampler.stop() if sampler else None
+    step_bytes = 2 * BATCH_BLOCKS * BLOCK_PAYLOAD
+    value = world * args.steps * step_bytes / (elapsed_ms / 1e3) / GB
+    dom, kernels, nvlink_achieved = _nvlink_roofline(torch, dist, device, timing, c0, c1, BLOCK_PAYLOAD)
+
+    # e2e: the public sharded API with host key / block-table arrays, wall clock (max over ranks)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        one_step(5000 + k)
+    store.flush()
+    torch.cuda.synchronize()
+    e2e_s = _max_over_ranks(torch, dist, time.perf_counter() - t0, device)
+    e2e = world * args.steps * step_bytes / e2e_s / GB
+
+    # latency: one collective step in which every rank gets one committed block
+    one_step(9000)
+    store.flush()
+    keys, dst = prev["keys"], np.arange(BATCH_BLOCKS, 2 * BATCH_BLOCKS, dtype=np.int64)
+    lat = []
+    for i in range(args.latency_samples):
+        j = i % BATCH_BLOCKS
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        ok = store.step(keys[j:j + 1], dst[j:j + 1])
+        torch.cuda.synchronize()
+        lat.append((time.perf_counter() - t1) * 1e3)
+        assert ok.all()
+    lat.sort()
+    p50 = lat[len(lat) // 2]
+    p99 = lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)]
+    pcie = _pcie_d2h_peak(torch, device)
+    stats = store.stats()
+    rounds = (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps
+    store.close()
+    if rank != 0:
+        return None
+    hbm_peak, peak_kind = measured_peaks()
+    k = kernels[dom]
+    return {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) bf16 KV, random block tables, 64-bit chained prefix-hash keys",
+        "config": {
+            "workload": WORKLOAD,
+            "layers": LAYERS, "kv_heads": HEADS, "head_dim": HEAD_DIM, "block_tokens": BLOCK_TOKENS,
+            "pool_blocks": POOL_BLOCKS, "blocks_per_step": BATCH_BLOCKS, "bytes_per_block": BLOCK_PAYLOAD,
+            "step": (f"every rank: get the {BATCH_BLOCKS} blocks it put in the previous step (100% device hit) "
+                     f"and put {BATCH_BLOCKS} fresh blocks, keys hash-sharded over {world} GPUs"),
+            "l2": f"inputs larger than L2 ({BATCH_BLOCKS * BLOCK_PAYLOAD / 2**30:.2f} GiB per direction per rank per step)",
+            "parallelism": f"hash-sharded store over {world} GPUs, transport {args.transport}",
+            "slab_bytes": slab_values * block_units * UNIT_BYTES,
+        },
+        "e2e": {"value": round(e2e, 3), "unit": UNIT,
+                "h2d_bytes_per_step": 2 * 8 * world * sharded.request_words(BATCH_BLOCKS),
+                "d2h_bytes_per_step": 2 * 8 * world * sharded.reply_words(BATCH_BLOCKS)},
+        "gpu_launches": int(launches),
+        "roofline": {
+            "kernel": dom, "bound": "nvlink", "achieved": round(nvlink_achieved, 1), "peak": NVLINK_PEER_GBS,
+            "unit": "GB/s", "frac": round(nvlink_achieved / NVLINK_PEER_GBS, 4),
+            "peak_kind": "measured peer copy per direction (pool figure)", "traffic": None,
+            "algorithmic_bytes_per_launch": k["nvlink_bytes_per_launch"], "avg_launch_ms": k["avg_ms"],
+            "hbm_peak": hbm_peak, "hbm_peak_kind": peak_kind,
+        },
+        "kernels": kernels,
+        "write_through": {
+            "bytes_per_step_per_gpu": BATCH_BLOCKS * BLOCK_PAYLOAD,
+            "achieved_GBps_per_gpu": round(BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB, 2),
+            "pcie_d2h_peak_GBps": round(pcie, 2),
+            "note": "every put is written through to the owner's pinned host tier; the next step's gets wait for it",
+        },
+        "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
+                                     "samples": len(lat), "note": "one collective step, every rank gets one block"},
+        "grant_rounds_per_step": rounds,
+        "store": {k2: stats[k2] for k2 in ("writes_through", "victims_evicted", "catalog_replacements", "live_keys")},
+        "clocks": clocks,
+    }
+
+
+# config-1 KV shape for the hash-sharded get/put mix
+MIX_LAYERS, MIX_HEADS, MIX_DIM, MIX_BT, MIX_POOL = 2, 8, 128, 32, 1024
+MIX_BATCH, MIX_GETS = 256, 179  # 70 / 30 get / put
+MIX_PAYLOAD = 2 * MIX_LAYERS * MIX_HEADS * MIX_BT * MIX_DIM * 2  # 256 KiB
+
+
+def _splitmix64(x: np.ndarray) -> np.ndarray:
+    z = (x + np.uint64(0x9E3779B97F4A7C15)).astype(np.uint64)
+    z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+    z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return z ^ (z >> np.uint64(31))
+
+
+def run_mix(args, rank, local_rank, world):
+    """Hash-sharded store over N GPUs with `resident` blocks per GPU; every rank issues 256-block
+    batches of 179 gets (uniform over every rank's resident keys) and 77 puts (overwrites of its
+    own keys), targets uniform over shards; timed once with P2P stores and once with NCCL
+    send/recv of packed values on the same store."""
+    import torch
+    import torch.distributed as dist
+
+    from kvcache_manager import PagedLayout, sharded
+
+    device = local_rank
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device)
+    g.manual_seed(77 + rank)
+    members = [torch.empty((MIX_POOL, MIX_HEADS, MIX_BT, MIX_DIM), dtype=torch.bfloat16, device=device).normal_(generator=g)
+               for _ in range(2 * MIX_LAYERS)]
+    layout = PagedLayout(members, members_per_layer=2)
+    vlen = layout.value_bytes()
+    units = -(-vlen // UNIT_BYTES)
+    block_units = 1 << (units - 1).bit_length()
+    R = args.resident or min((1 << 20) // world, 16384)
+    max_keys = R + R // 8 + 1024
+    store = sharded.create(layout, max_batch=MIX_BATCH, transport="p2p", max_keys=max_keys,
+                           heap_bytes=max_keys * block_units * UNIT_BYTES,
+                           host_pool_bytes=max_keys * units * UNIT_BYTES)
+    eng = store.engine
+    rng = np.random.default_rng(500 + rank)
+
+    def key(r, i):
+        return _splitmix64((np.uint64(r) << np.uint64(40)) | np.asarray(i, np.uint64))
+
+    # populate: every rank puts its R keys (the blocks land on their owners over NVLink)
+    t_pop = time.perf_counter()
+    for b0 in range(0, R, MIX_BATCH):
+        ids = np.arange(b0, min(R, b0 + MIX_BATCH))
+        store.step((), (), key(rank, ids), (ids % MIX_POOL).astype(np.int64))
+    store.flush()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t_pop = time.perf_counter() - t_pop
+
+    def one_step():
+        perm = rng.permutation(MIX_POOL)
+        gr = rng.integers(0, world, MIX_GETS)
+        gk = _splitmix64((gr.astype(np.uint64) << np.uint64(40)) | rng.integers(0, R, MIX_GETS).astype(np.uint64))
+        pk = key(rank, rng.choice(R, MIX_BATCH - MIX_GETS, replace=False))
+        found = store.step(gk, perm[:MIX_GETS].astype(np.int64), pk, perm[MIX_GETS:MIX_BATCH].astype(np.int64))
+        if not found.all():
+            raise RuntimeError(f"rank {rank}: {int((~found).sum())} resident blocks missed")
+
+    results = {}
+    for transport in ("p2p", "nccl"):
+        store.transport = transport
+        for _ in range(args.warmup):
+            one_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        eng.client.kernel_timing()
+        eng.client.set_kernel_timing(True)
+        c0 = dict(store.counters)
+        stream = torch.cuda.current_stream(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler = ClockSampler([device]) if rank == 0 else None
+        if sampler:
+            sampler.start()
+        torch.cuda.synchronize()
+        dist.barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            one_step()
+        store.flush()
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = _max_over_ranks(torch, dist, start.elapsed_time(end), device)
+        timing = eng.client.kernel_timing()
+        eng.client.set_kernel_timing(False)
+        c1 = dict(store.counters)
+        clocks = sampler.stop() if sampler else None
+        moved = _sum_over_ranks(torch, dist, (c1["gets_found"] - c0["gets_found"] + c1["puts"] - c0["puts"]) * MIX_PAYLOAD,
+                                device)
+        dom, kernels, nvl = _nvlink_roofline(torch, dist, device, timing, c0, c1, MIX_PAYLOAD)
+        results[transport] = {"value": round(moved / (ms / 1e3) / GB, 3), "ms_per_step": round(ms / args.steps, 3),
+                              "kernels": kernels, "roofline_kernel": dom,
+                              "nvlink_achieved_GBps": round(nvl, 1),
+                              "nvlink_frac": round(nvl / NVLINK_PEER_GBS, 4), "clocks": clocks,
+                              "grant_rounds_per_step": (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps}
+    stats = store.stats()
+    store.close()
+    if rank != 0:
+        return None
+    p = results["p2p"]
+    return {
+        "metric": METRIC, "value": p["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": p["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) bf16 KV, 64-bit splitmix keys, uniform targets",
+        "config": {"workload": "hash-sharded-config1-kv-70-30-get-put-256blk", "layers": MIX_LAYERS,
+                   "kv_heads": MIX_HEADS, "head_dim": MIX_DIM, "block_tokens": MIX_BT, "pool_blocks": MIX_POOL,
+                   "bytes_per_block": MIX_PAYLOAD, "batch": f"{MIX_GETS} gets + {MIX_BATCH - MIX_GETS} puts per rank",
+                   "resident_blocks_per_gpu": R, "resident_blocks_total": R * world,
+                   "populate_s": round(t_pop, 2), "parallelism": f"hash-sharded store over {world} GPUs"},
+        "transports": results,
+        "store": {k: stats[k] for k in ("live_keys", "device_resident_keys", "writes_through", "victims_evicted")},
+    }
 
 
 # ------------------------------------------------------------------ CPU baseline (the oracle)
@@ -616,6 +961,9 @@ def main():
         print(json.dumps(run_sweep(args) if args.sweep else run_multiturn(args)))
         return
     rank, local_rank, world = dist_env()
+    if args.mix and world == 1:
+        print(json.dumps({"error": "--mix shards the store over N > 1 GPUs: run it under torchrun"}))
+        sys.exit(2)
     if world != args.gpus and world == 1 and args.gpus > 1:
         print(json.dumps({"error": "run N>1 under torchrun (one rank per GPU)"}))
         sys.exit(2)
@@ -631,7 +979,12 @@ def main():
             torch.cuda.set_device(local_rank)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                     device_id=torch.device("cuda", local_rank))
-        line = run_ours(args, rank, local_rank, world)
+        if args.mix:
+            line = run_mix(args, rank, local_rank, world)
+        elif world > 1 and args.parallelism == "sharded":
+            line = run_sharded(args, rank, local_rank, world)
+        else:
+            line = run_ours(args, rank, local_rank, world)
         if world > 1:
             import torch.distributed as dist
 

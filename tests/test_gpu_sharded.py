@@ -118,13 +118,15 @@ def _run_ranks(rank, world, port, transport, steps, batch, q):
         pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=5)
         members, layout = _gpu_pool(pools[rank], f"cuda:{rank}")
         store = sharded.create(layout, max_batch=batch, transport=transport, **CFG)
-        found = []
+        found, snaps = [], []
         for row in plan:
             gk, gi, pk, pi = row[rank]
             found.append(store.step(gk, gi, pk, pi))
+            torch.cuda.synchronize()
+            snaps.append(_host(members))
         store.flush()
         torch.cuda.synchronize()
-        out = (rank, _host(members), found, store.stats())
+        out = (rank, snaps, found, store.stats())
         store.close()
         store = None
         q.put(out)
@@ -135,12 +137,29 @@ def _run_ranks(rank, world, port, transport, steps, batch, q):
 def _check_against_replay(outs, world, steps, batch):
     plan = make_plan(world, steps, N_POOL, batch, seed=31)
     pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=5)
-    exp_pools, exp_found, exp_stats = replay(plan, pools, MB, CFG)
-    for rank, members, found, stats in outs:
-        for m in range(N_MEMBERS):
-            assert np.array_equal(members[m], exp_pools[rank][m]), f"rank {rank} member {m}"
-        for s in range(steps):
-            assert np.array_equal(found[s], exp_found[s][rank]), f"rank {rank} step {s}"
+    for s, (exp_pools, exp_found, exp_stats) in enumerate(replay_steps(plan, pools, MB, CFG)):
+        for rank, snaps, found, _ in outs:
+            assert np.array_equal(found[s], exp_found[rank]), f"rank {rank} step {s}"
+            for m in range(N_MEMBERS):
+                got = snaps[s][m].reshape(N_POOL, MB)
+                bad = np.flatnonzero((got != exp_pools[rank][m].reshape(N_POOL, MB)).any(1))
+                origin = []
+                for b in bad[:2]:
+                    # where the delivered bytes came from: a block of some rank's initial pool?
+                    for r2 in range(world):
+                        src = pools[r2][m].reshape(N_POOL, MB)
+                        hit = np.flatnonzero((src == got[b]).all(1))
+                        if hit.size:
+                            origin.append((int(b), r2, hit.tolist()))
+                    nz = int(np.count_nonzero(got[b] != exp_pools[rank][m].reshape(N_POOL, MB)[b]))
+                    origin.append((int(b), "bytes differing", nz, "first", got[b][:8].tolist(),
+                                   exp_pools[rank][m].reshape(N_POOL, MB)[b][:8].tolist()))
+                assert bad.size == 0, (
+                    f"origin {origin}; "
+                    f"step {s} rank {rank} member {m}: blocks {bad.tolist()} differ; this rank's gets "
+                    f"{list(zip(plan[s][rank][0].tolist(), plan[s][rank][1].tolist(), found[s].tolist()))}; "
+                    f"puts {list(zip(plan[s][rank][2].tolist(), plan[s][rank][3].tolist()))}")
+    for rank, _, _, stats in outs:
         for f in STAT_FIELDS:
             assert stats[f] == exp_stats[rank][f], (rank, f, stats[f], exp_stats[rank][f])
 

@@ -300,6 +300,10 @@ class ShardedStore:
         self._rows_out = None
         self._rows_in = None
         self.steps = 0
+        # blocks moved by this rank: as a client (puts sent, gets found) and as an owner (gets
+        # served); "remote" ones crossed to or from another GPU
+        self.counters = dict(puts=0, puts_remote=0, gets=0, gets_found=0, served=0, served_remote=0,
+                             grant_rounds=0)
         self.closed = False
 
     # ---- collectives
@@ -346,6 +350,11 @@ class ShardedStore:
         if ops:
             for w in dist.batch_isend_irecv(ops):
                 w.wait()
+            if self._cuda:
+                # the work handles of a batched send/recv do not order this process's later
+                # streams after the transfer (a copy launched next read the rows before they
+                # arrived); a device synchronize does
+                self._torch.cuda.synchronize(self._dev)
 
     # ---- public API
     def step(self, get_keys: Any = (), get_ids: Any = (), put_keys: Any = (), put_ids: Any = ()) -> np.ndarray:
@@ -372,6 +381,9 @@ class ShardedStore:
         else:
             out_rows = self._rows("_rows_out", g_keys.size)
             found = eng.serve_gets_packed(g_keys, out_rows[:g_keys.size])
+        c = self.counters
+        c["served"] += int(found.sum())
+        c["served_remote"] += int(found[g_sets != self.rank].sum())
         # ---- owner: first round of put grants
         put_keys_by_src = [r[2] for r in reqs]
         put_ids_by_src = [r[3] for r in reqs]
@@ -414,9 +426,14 @@ class ShardedStore:
             # rows of misses hold nothing: scatter the hits only
             sel = np.flatnonzero(my_found[order])
             eng.scatter_rows(gi[order][sel], in_rows, sel)
+        c["gets"] += gk.size
+        c["gets_found"] += int(my_found.sum())
+        c["puts"] += pk.size
+        c["puts_remote"] += int(sum(p_pos[o].size for o in range(world) if o != self.rank))
         # ---- put rounds
         p_cursor = [0] * world  # per owner: puts of this rank granted so far
         while True:
+            c["grant_rounds"] += 1
             ids, owners, offs, counts = [], [], [], [0] * world
             for o in range(world):
                 ng = int(back[o, 2])
