@@ -404,19 +404,31 @@ def _sum_over_ranks(torch, dist, value, device):
     return float(t.item())
 
 
-def _pcie_d2h_peak(torch, device):
-    pin = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
-    src_buf = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+def _host_write_rates(torch, dist, device, chunks=128, chunk=16 << 20):
+    """Device->host copy rate of every rank while all ranks copy at once (barrier-aligned): the
+    write-through ceiling of the box. 128 x 16 MiB copies into a 2 GiB pinned buffer per rank.
+    Returns (this rank's GB/s, min over ranks, sum over ranks)."""
+    pin = torch.empty(chunks * chunk, dtype=torch.uint8, pin_memory=True)
+    src = torch.empty(chunk, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
     best = 0.0
-    for _ in range(3):
+    for _ in range(2):
+        torch.cuda.synchronize()
+        dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        pin.copy_(src_buf, non_blocking=True)
+        for i in range(chunks):
+            pin[i * chunk:(i + 1) * chunk].copy_(src, non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize()
-        best = max(best, (1 << 30) / (e0.elapsed_time(e1) / 1e3) / GB)
-    return best
+        best = max(best, chunks * chunk / (e0.elapsed_time(e1) / 1e3) / GB)
+    del pin, src
+    t = torch.tensor([best, -best, best], device=device, dtype=torch.float64)
+    lo = t[1:2].clone()
+    dist.all_reduce(lo, op=dist.ReduceOp.MAX)
+    tot = t[2:3].clone()
+    dist.all_reduce(tot)
+    return best, -float(lo.item()), float(tot.item())
 
 
 def _nvlink_roofline(torch, dist, device, timing, counters0, counters1, payload):
@@ -549,10 +561,11 @@ def run_sharded(args, rank, local_rank, world):
     lat.sort()
     p50 = lat[len(lat) // 2]
     p99 = lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)]
-    pcie = _pcie_d2h_peak(torch, device)
     stats = store.stats()
     rounds = (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps
     store.close()
+    hw_mine, hw_min, hw_sum = _host_write_rates(torch, dist, device)
+    wt_per_gpu = BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB
     if rank != 0:
         return None
     hbm_peak, peak_kind = measured_peaks()
@@ -586,9 +599,12 @@ def run_sharded(args, rank, local_rank, world):
         "kernels": kernels,
         "write_through": {
             "bytes_per_step_per_gpu": BATCH_BLOCKS * BLOCK_PAYLOAD,
-            "achieved_GBps_per_gpu": round(BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB, 2),
-            "pcie_d2h_peak_GBps": round(pcie, 2),
-            "note": "every put is written through to the owner's pinned host tier; the next step's gets wait for it",
+            "achieved_GBps_per_gpu": round(wt_per_gpu, 2),
+            "concurrent_d2h_GBps_per_gpu": {"rank0": round(hw_mine, 2), "min": round(hw_min, 2)},
+            "concurrent_d2h_GBps_all_gpus": round(hw_sum, 1),
+            "frac_of_slowest_gpu": round(wt_per_gpu / hw_min, 4),
+            "note": ("every put is written through to the owner's pinned host tier and the next step's gets wait "
+                     "for it: the step is bound by the slowest GPU's device->host rate while all GPUs copy at once"),
         },
         "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
                                      "samples": len(lat), "note": "one collective step, every rank gets one block"},
@@ -699,6 +715,7 @@ def run_mix(args, rank, local_rank, world):
                               "grant_rounds_per_step": (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps}
     stats = store.stats()
     store.close()
+    hw_mine, hw_min, hw_sum = _host_write_rates(torch, dist, device)
     if rank != 0:
         return None
     p = results["p2p"]
@@ -713,6 +730,8 @@ def run_mix(args, rank, local_rank, world):
                    "resident_blocks_per_gpu": R, "resident_blocks_total": R * world,
                    "populate_s": round(t_pop, 2), "parallelism": f"hash-sharded store over {world} GPUs"},
         "transports": results,
+        "concurrent_d2h_GBps_per_gpu": {"rank0": round(hw_mine, 2), "min": round(hw_min, 2),
+                                        "all_gpus": round(hw_sum, 1)},
         "store": {k: stats[k] for k in ("live_keys", "device_resident_keys", "writes_through", "victims_evicted")},
     }
 
