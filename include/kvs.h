@@ -17,7 +17,11 @@
  *   - Keys are 1..max_key_bytes (<= 128) bytes. The batched block calls take 64-bit keys
  *     (chained prefix-block hashes); a 64-bit key is stored as its 8 little-endian bytes, so
  *     kvs_put(key=&u64, key_len=8) and kvs_put_blocks(keys={u64}) name the same entry.
- *   - Ordering follows the reference (design.md sections 5-6, patch 0003 lines 7527-7683): a put
+ *   - `stream` is the caller's stream: a call's device work starts after the work queued on it
+ *     before the call and work queued on it after the call starts after the call's device work.
+ *     A null stream is the legacy default stream (torch's default stream).
+ *   - Ordering follows the reference (kvcache_manager/docs/design.md sections 5-6 in patch 0003,
+ *     lines 7527-7683): a put
  *     returns once its bytes have landed in the device slab (on `stream`); host write-through
  *     finishes asynchronously; get, exists, delete, move and flush first wait for every issued
  *     put to be host-committed (the reference's COMMIT_BARRIER).

@@ -288,6 +288,53 @@ struct kvs_server {
   void release_dropped() {
     for (auto &b : dir->take_dropped()) release_backing(b);
   }
+  // Device->host copies of one write-through batch, coalesced: consecutive values of one length
+  // whose slab blocks are evenly spaced and whose host extents are evenly spaced become one 2-D
+  // copy, so a large put issues a handful of copy commands instead of one per value (thousands of
+  // queued copies would block the issuing thread until the copy queue drains).
+  struct WtRun {
+    uint8_t *host;
+    const uint8_t *slab;
+    uint64_t len, host_pitch, slab_pitch, n;
+  };
+  std::vector<WtRun> wt_runs;
+  bool in_pool(const uint8_t *p) const {
+    return pool && p >= pool && p < pool + (cfg.host_pool_bytes / cfg.unit_bytes) * cfg.unit_bytes;
+  }
+  static constexpr uint64_t kWtMergeBelow = 8ull << 20;  // large values already make few commands
+  void wt_add(uint8_t *host, const uint8_t *slab_ptr, uint64_t len) {
+    // a 2-D copy spans the rows between its ends: merge only inside the one pinned pool allocation
+    if (!wt_runs.empty() && len < kWtMergeBelow && in_pool(host) && in_pool(wt_runs.back().host)) {
+      WtRun &r = wt_runs.back();
+      if (r.len == len) {
+        const uint8_t *last_slab = r.slab + (r.n - 1) * r.slab_pitch;
+        uint8_t *last_host = r.host + (r.n - 1) * r.host_pitch;
+        if (r.n == 1 && slab_ptr > r.slab && host > r.host && (uint64_t)(slab_ptr - r.slab) >= len &&
+            (uint64_t)(host - r.host) >= len) {
+          r.slab_pitch = (uint64_t)(slab_ptr - r.slab);
+          r.host_pitch = (uint64_t)(host - r.host);
+          r.n = 2;
+          return;
+        }
+        if (r.n > 1 && slab_ptr == last_slab + r.slab_pitch && host == last_host + r.host_pitch) {
+          r.n++;
+          return;
+        }
+      }
+    }
+    wt_runs.push_back({host, slab_ptr, len, len, len, 1});
+  }
+  int wt_issue() {
+    for (const WtRun &r : wt_runs) {
+      if (r.n == 1)
+        CUDA_TRY(cudaMemcpyAsync(r.host, r.slab, r.len, cudaMemcpyDeviceToHost, wt_stream));
+      else
+        CUDA_TRY(cudaMemcpy2DAsync(r.host, r.host_pitch, r.slab, r.slab_pitch, r.len, r.n, cudaMemcpyDeviceToHost,
+                                   wt_stream));
+    }
+    wt_runs.clear();
+    return KVS_OK;
+  }
   // Commit the FIFO head, waiting for its device->host copy.
   int commit_one() {
     auto &head = dir->fifo_head();
@@ -468,19 +515,17 @@ struct ShardLocks {
   }
 };
 
+// The client stream is non-blocking, so it is ordered with the caller's stream explicitly at entry
+// and exit. A null handle is the legacy default stream (torch's default stream), not "no stream".
 int begin_op(kvs_client *c, void *caller) {
-  if (caller) {
-    CUDA_TRY(cudaEventRecord(c->entry_evt, (cudaStream_t)caller));
-    CUDA_TRY(cudaStreamWaitEvent(c->stream, c->entry_evt, 0));
-  }
+  CUDA_TRY(cudaEventRecord(c->entry_evt, (cudaStream_t)caller));
+  CUDA_TRY(cudaStreamWaitEvent(c->stream, c->entry_evt, 0));
   return KVS_OK;
 }
 
 int end_op(kvs_client *c, void *caller) {
-  if (caller) {
-    CUDA_TRY(cudaEventRecord(c->exit_evt, c->stream));
-    CUDA_TRY(cudaStreamWaitEvent((cudaStream_t)caller, c->exit_evt, 0));
-  }
+  CUDA_TRY(cudaEventRecord(c->exit_evt, c->stream));
+  CUDA_TRY(cudaStreamWaitEvent((cudaStream_t)caller, c->exit_evt, 0));
   return KVS_OK;
 }
 
@@ -765,9 +810,9 @@ int flush_puts(PutBatch &b, cudaStream_t) {
       const uint64_t len = s->dir->entry(pp.slot).total_len;
       TRY(s->reserve_backing(len, &pp.backing));
       pp.wt_batch = (int)batch_id;
-      CUDA_TRY(cudaMemcpyAsync(s->host_ptr(pp.backing), s->slab + it.slab_off, len, cudaMemcpyDeviceToHost,
-                               s->wt_stream));
+      s->wt_add(s->host_ptr(pp.backing), s->slab + it.slab_off, len);
     }
+    TRY(s->wt_issue());
     CUDA_TRY(cudaEventRecord(ev, s->wt_stream));
   }
   c->prof.program_ns += t1 - t0;
@@ -1166,7 +1211,7 @@ int kvs_client_destroy(kvs_client *c) {
     std::lock_guard<std::mutex> lk(c->mu);
     DeviceGuard g(c->device);
     if (!c->closed && !c->quarantined && c->stream) {
-      // drain every issued put of this client's shards (Client::close, design.md section 8)
+      // drain every issued put of this client's shards (Client::close; kvcache_manager/docs/design.md section 8 in patch 0003)
       std::vector<uint8_t> inv(c->shards.size(), 1);
       ShardLocks locks(involved_servers(c, inv));
       rc = commit_barrier(c, inv);
@@ -2139,9 +2184,9 @@ int kvs_puts_landed(kvs_client *c, void *stream) {
     const kvs::Entry &e = s->dir->entry(pp.slot);
     TRY(s->reserve_backing(e.total_len, &pp.backing));
     pp.wt_batch = (int)batch_id;
-    CUDA_TRY(cudaMemcpyAsync(s->host_ptr(pp.backing), s->slab + e.value_off, e.total_len, cudaMemcpyDeviceToHost,
-                             s->wt_stream));
+    s->wt_add(s->host_ptr(pp.backing), s->slab + e.value_off, e.total_len);
   }
+  TRY(s->wt_issue());
   CUDA_TRY(cudaEventRecord(ev, s->wt_stream));
   s->unlanded = 0;
   return KVS_OK;
