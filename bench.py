@@ -907,25 +907,34 @@ def multiturn_plan(n_sessions, n_turns, seed=3, lo=512, hi=4096, block_tokens=32
     return plan
 
 
-def run_multiturn_workload(client, layout, plan, pool_blocks, seed=3, on_turn=None):
+def run_multiturn_workload(client, layout, plan, pool_blocks, seed=3, on_turn=None, phase_s=None):
     """Each turn: exists on the prompt's blocks, get the longest contiguous prefix of hits, put the
-    rest. Block keys are chained prefix hashes per session, so turn t+1 shares turn t's prefix."""
+    rest. Block keys are chained prefix hashes per session, so turn t+1 shares turn t's prefix.
+    phase_s (optional dict): host wall seconds spent in each call kind."""
     from kvcache_manager import codec
 
     rng = np.random.default_rng(seed + 1)
     stats = {"blocks": 0, "prefix_hits": 0, "puts": 0, "gets": 0}
     order = [(t, s) for t in range(len(plan[0])) for s in range(len(plan))]  # sessions interleave by turn
+    clock = time.perf_counter
     for t, s in order:
         n = plan[s][t]
         keys = np.array(codec.chained_block_hashes(1_000_003 * (s + 1), n), np.uint64)
+        t0 = clock()
         found = client.exists_batch(keys)
+        t1 = clock()
         hit = int(np.argmin(found)) if not found.all() else n
         slots = rng.permutation(pool_blocks)[:n]
         if hit:
             got = client.get_blocks(layout, keys[:hit], slots[:hit])
             assert got.all(), "a prefix block reported by exists was not restored"
+        t2 = clock()
         if hit < n:
             client.put_blocks(layout, keys[hit:], slots[hit:])
+        t3 = clock()
+        if phase_s is not None:
+            for k, v in (("exists", t1 - t0), ("get", t2 - t1), ("put", t3 - t2)):
+                phase_s[k] = phase_s.get(k, 0.0) + v
         stats["blocks"] += n
         stats["prefix_hits"] += hit
         stats["gets"] += hit
@@ -956,8 +965,9 @@ def run_multiturn(args):
     server = Server(0, max_keys=2 * working_set, heap_bytes=slab, host_pool_bytes=(working_set + 64) * units * UNIT_BYTES)
     client = Client(0, server)
     torch.cuda.synchronize()
+    phase = {}
     t0 = time.perf_counter()
-    st = run_multiturn_workload(client, layout, plan, pool)
+    st = run_multiturn_workload(client, layout, plan, pool, phase_s=phase)
     client.flush()
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
@@ -971,7 +981,9 @@ def run_multiturn(args):
             "prefix_hit_rate": round(st["prefix_hits"] / max(1, st["blocks"]), 4),
             "host_tier_serves": sst["host_serves"], "admissions": sst["admissions"],
             "victims_evicted": sst["victims_evicted"],
-            "moved_GBps": round((st["gets"] + st["puts"]) * payload / dt / GB, 3)}
+            "moved_GBps": round((st["gets"] + st["puts"]) * payload / dt / GB, 3),
+            "host_s_by_call": {k: round(v, 4) for k, v in phase.items()},
+            "pcie_bytes": {"h2d_admissions": sst["admissions"] * vlen, "d2h_write_through": sst["writes_through"] * vlen}}
 
 
 def main():

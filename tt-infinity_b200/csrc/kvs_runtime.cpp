@@ -385,6 +385,7 @@ struct kvs_client {
   cudaEvent_t entry_evt = nullptr, exit_evt = nullptr, landed_evt = nullptr;
   std::vector<cudaEvent_t> chain_evt;  // per shard
   Staging stage;
+  Staging stage2;  // a get's second pass, packed while the first pass's results are still in flight
   bool closed = false, quarantined = false;
   kvs_put_profile prof{};
   std::vector<uint64_t> validated_members;
@@ -594,13 +595,14 @@ size_t mutation_upper_bound(kvs_server *s) {
   return 16 * nb + 24 * nm + 4ull * (kvs::kKeyRowWords + 1) * nk + 64;
 }
 
-int launch_mutations(kvs_client *c, kvs_server *s, const PackedMutations &pm) {
+int launch_mutations(kvs_client *c, kvs_server *s, const PackedMutations &pm, Staging *from = nullptr) {
+  Staging &st = from ? *from : c->stage;
   kvs::MutationParams mp{};
-  mp.bucket_writes = c->stage.d<uint64_t>(pm.buckets_off);
+  mp.bucket_writes = st.d<uint64_t>(pm.buckets_off);
   mp.n_bucket_writes = pm.nb;
-  mp.meta_writes = c->stage.d<uint64_t>(pm.meta_off);
+  mp.meta_writes = st.d<uint64_t>(pm.meta_off);
   mp.n_meta_writes = pm.nm;
-  mp.key_writes = c->stage.d<uint32_t>(pm.keys_off);
+  mp.key_writes = st.d<uint32_t>(pm.keys_off);
   mp.n_key_writes = pm.nk;
   mp.buckets = s->d_buckets;
   mp.meta = s->d_meta;
@@ -1196,7 +1198,7 @@ int kvs_client_create(kvs_server *const *shards, uint32_t n_shards, int32_t devi
   c->chain_evt.assign(n_shards, nullptr);
   for (uint32_t i = 0; i < n_shards && e == cudaSuccess; ++i)
     e = cudaEventCreateWithFlags(&c->chain_evt[i], cudaEventDisableTiming);
-  if (e != cudaSuccess || c->stage.init() != KVS_OK) {
+  if (e != cudaSuccess || c->stage.init() != KVS_OK || c->stage2.init() != KVS_OK) {
     kvs_client_destroy(c);
     return set_err(KVS_E_CUDA, "client init: %s", cudaGetErrorString(e));
   }
@@ -1233,6 +1235,7 @@ int kvs_client_destroy(kvs_client *c) {
     for (auto e : c->event_pool) cudaEventDestroy(e);
     if (c->timeout_flag) cudaFreeHost(c->timeout_flag);
     c->stage.release();
+    c->stage2.release();
     for (auto e : c->chain_evt)
       if (e) cudaEventDestroy(e);
     if (c->entry_evt) cudaEventDestroy(c->entry_evt);
@@ -1706,23 +1709,28 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
     if (inv[i]) c->shards[i]->launches++;
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) TRY(chain_record(c, i));
-  // while the GPU works: the authoritative host lookups
+  // While the GPU works: the authoritative host lookups decide every outcome (the device replica
+  // mirrors the catalog, so a key the catalog places on the host tier is one pass 1 did not
+  // deliver). The device results are checked against them once, after the last pass.
   std::vector<uint32_t> host_slot(n);
-  for (uint32_t i = 0; i < n; ++i) host_slot[i] = c->shards[si[i]]->dir->lookup((const uint8_t *)&keys[i], 8);
-  CUDA_TRY(cudaStreamSynchronize(c->stream));
-  TRY(quarantine_on_error(c, check_tma_timeouts(c, "get_blocks")));
   std::vector<kvs::LookupOut> res(n);
-  for (uint32_t j = 0; j < n; ++j) res[ord.perm[j]] = st.h<kvs::LookupOut>(out_off)[j];
-  int format_error = -1;
   for (uint32_t i = 0; i < n; ++i) {
-    const bool dev_hit = res[i].status != kvs::kMiss;
-    const bool host_hit = host_slot[i] != kvs::kBucketEmpty;
-    if (dev_hit != host_hit || (dev_hit && res[i].slot != host_slot[i])) {
-      c->quarantined = true;
-      return set_err(KVS_E_CUDA, "get_blocks: device index replica disagrees with the catalog for key %u", i);
-    }
-    if (res[i].status == kvs::kLenMismatch && format_error < 0) format_error = (int)i;
+    kvs_server *s = c->shards[si[i]];
+    host_slot[i] = s->dir->lookup((const uint8_t *)&keys[i], 8);
+    kvs::LookupOut &r = res[i];
+    r.status = kvs::kMiss;
+    r.slot = host_slot[i];
+    if (host_slot[i] == kvs::kBucketEmpty) continue;
+    const kvs::Entry &e = s->dir->entry(host_slot[i]);
+    r.value_len = (uint32_t)e.total_len;
+    if (e.total_len != fmt.value_len)
+      r.status = kvs::kLenMismatch;
+    else
+      r.status = e.location == kvs::kLocHost ? kvs::kHitHost : kvs::kHitDevice;
   }
+  int format_error = -1;
+  for (uint32_t i = 0; i < n && format_error < 0; ++i)
+    if (res[i].status == kvs::kLenMismatch) format_error = (int)i;
   if (c->timing && !c->timed.empty() && c->timed.back().kind == 1) {
     uint64_t hits = 0;
     for (uint32_t i = 0; i < n; ++i) hits += res[i].status == kvs::kHitDevice;
@@ -1778,63 +1786,117 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
     late.push_back(L);
   }
   if (!late.empty()) {
-    // ---- pass 2: replica update, admissions (host -> slab), scatter of host-tier hits
-    size_t need2 = 4096 + 36ull * late.size() + ptr_bytes + 32ull * t.n_members;
+    // ---- pass 2, queued behind pass 1 on the client stream from the second staging area:
+    // replica update, admissions (host -> slab), scatter of host-tier hits
+    Staging &st2 = c->stage2;
+    size_t need2 = 4096 + 72ull * late.size() + ptr_bytes + 32ull * t.n_members;
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) need2 += mutation_upper_bound(c->shards[i]);
-    TRY(st.begin(need2, c->stream));
+    TRY(st2.begin(need2, c->stream));
     std::vector<PackedMutations> pms2(ns);
     for (size_t i = 0; i < ns; ++i)
-      if (inv[i]) pms2[i] = pack_mutations(c->shards[i], st);
+      if (inv[i]) pms2[i] = pack_mutations(c->shards[i], st2);
     size_t nscatter = 0;
     for (auto &L : late) nscatter += L.scatter;
-    const size_t blobs2 = st.take(8 * std::max<size_t>(nscatter, 1));
-    const size_t ids2 = st.take(8 * std::max<size_t>(nscatter, 1));
-    const size_t sets2 = st.take(4 * std::max<size_t>(nscatter, 1));
+    const size_t blobs2 = st2.take(8 * std::max<size_t>(nscatter, 1));
+    const size_t ids2 = st2.take(8 * std::max<size_t>(nscatter, 1));
+    const size_t sets2 = st2.take(4 * std::max<size_t>(nscatter, 1));
     size_t k = 0;
     for (auto &L : late)
       if (L.scatter) {
         // values in the slab (admitted in this batch) are scattered from their block, others
         // from host memory
-        st.h<uint64_t>(blobs2)[k] = L.slab_src ? L.slab_src : L.host_dev;
-        st.h<int64_t>(ids2)[k] = block_ids[L.i];
-        st.h<uint32_t>(sets2)[k] = t.sets ? t.sets[L.i] : 0;
+        st2.h<uint64_t>(blobs2)[k] = L.slab_src ? L.slab_src : L.host_dev;
+        st2.h<int64_t>(ids2)[k] = block_ids[L.i];
+        st2.h<uint32_t>(sets2)[k] = t.sets ? t.sets[L.i] : 0;
         ++k;
       }
-    const size_t mp2 = st.push(t.member_ptrs, ptr_bytes);
-    const size_t mb2 = st.push(t.member_bytes, 8ull * t.n_members);
-    const size_t rb2 = st.push(fmt.region_bases.data(), 8ull * t.n_members);
-    const size_t tp2 = st.push(fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
-    TRY(st.upload(c->stream, st.used));
+    const size_t mp2 = st2.push(t.member_ptrs, ptr_bytes);
+    const size_t mb2 = st2.push(t.member_bytes, 8ull * t.n_members);
+    const size_t rb2 = st2.push(fmt.region_bases.data(), 8ull * t.n_members);
+    const size_t tp2 = st2.push(fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
+    // admissions as one copy list: value a goes from its pinned host copy (device alias) to its
+    // new slab block; each value is its own one-member set whose member pointer is the block
+    size_t n_admit = 0;
+    for (auto &L : late) n_admit += (L.admit_dst && L.host_dev);
+    const size_t adm_dst = st2.take(8 * std::max<size_t>(n_admit, 1));
+    const size_t adm_src = st2.take(8 * std::max<size_t>(n_admit, 1));
+    const size_t adm_set = st2.take(4 * std::max<size_t>(n_admit, 1));
+    const size_t adm_ids = st2.take(8 * std::max<size_t>(n_admit, 1));
+    const uint64_t adm_meta[5] = {fmt.value_len, 0, 0, (fmt.value_len + kTileBytes - 1) / kTileBytes, 0};
+    const size_t adm_m = st2.push(adm_meta, sizeof adm_meta);
+    {
+      size_t a = 0;
+      for (auto &L : late)
+        if (L.admit_dst && L.host_dev) {
+          st2.h<uint64_t>(adm_dst)[a] = L.admit_dst;
+          st2.h<uint64_t>(adm_src)[a] = L.host_dev;
+          st2.h<uint32_t>(adm_set)[a] = (uint32_t)a;
+          st2.h<int64_t>(adm_ids)[a] = 0;
+          ++a;
+        }
+    }
+    TRY(st2.upload(c->stream, st2.used));
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) TRY(chain_wait(c, c->shards[i]));
     for (size_t i = 0; i < ns; ++i)
-      if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms2[i])));
+      if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms2[i], &st2)));
+    if (n_admit) {
+      kvs::ChunkCopyParams a{};
+      a.member_ptrs = st2.d<uint64_t>(adm_dst);
+      a.blob_sets = st2.d<uint32_t>(adm_set);
+      a.member_bytes = st2.d<uint64_t>(adm_m);
+      a.region_bases = st2.d<uint64_t>(adm_m + 8);
+      a.tile_prefix = st2.d<uint64_t>(adm_m + 16);
+      a.block_ids = st2.d<int64_t>(adm_ids);
+      a.blob_ptrs = st2.d<uint64_t>(adm_src);
+      a.n_blobs = (uint32_t)n_admit;
+      a.blocks_per_blob = 1;
+      a.n_ranks = 1;
+      a.n_members = 1;
+      a.tile_bytes = kTileBytes;
+      a.tiles_per_combo = adm_meta[3];
+      a.total_tiles = (uint64_t)n_admit * a.tiles_per_combo;
+      a.to_blob = 0;
+      CUDA_TRY(launch_copy(a, c->stream, false, c->timeout_flag));  // the source is host memory
+    }
     for (auto &L : late)
-      if (L.admit_dst)
+      if (L.admit_dst && !L.host_dev)  // no device alias: a copy-engine copy
         CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<void *>(L.admit_dst), L.host, L.len, cudaMemcpyHostToDevice,
                                  c->stream));
     if (nscatter) {
       kvs::ChunkCopyParams q = p;
-      q.member_ptrs = st.d<uint64_t>(mp2);
-      q.blob_sets = t.sets ? st.d<uint32_t>(sets2) : nullptr;
-      q.member_bytes = st.d<uint64_t>(mb2);
-      q.region_bases = st.d<uint64_t>(rb2);
-      q.tile_prefix = st.d<uint64_t>(tp2);
-      q.block_ids = st.d<int64_t>(ids2);
-      q.blob_ptrs = st.d<uint64_t>(blobs2);
+      q.member_ptrs = st2.d<uint64_t>(mp2);
+      q.blob_sets = t.sets ? st2.d<uint32_t>(sets2) : nullptr;
+      q.member_bytes = st2.d<uint64_t>(mb2);
+      q.region_bases = st2.d<uint64_t>(rb2);
+      q.tile_prefix = st2.d<uint64_t>(tp2);
+      q.block_ids = st2.d<int64_t>(ids2);
+      q.blob_ptrs = st2.d<uint64_t>(blobs2);
       q.n_blobs = (uint32_t)nscatter;
       q.total_tiles = (uint64_t)nscatter * q.tiles_per_combo;
       CUDA_TRY(launch_copy(q, c->stream, false, c->timeout_flag));
     }
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) TRY(chain_record(c, i));
-    CUDA_TRY(cudaStreamSynchronize(c->stream));
     for (auto &L : late) {
       if (!L.moved) continue;
       kvs_server *s = c->shards[L.shard];
       s->mprof.to_device_count++;
       s->moves_completed.fetch_add(1, std::memory_order_relaxed);
+    }
+  }
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  TRY(quarantine_on_error(c, check_tma_timeouts(c, "get_blocks")));
+  // the device probe must have found exactly what the catalog holds
+  for (uint32_t j = 0; j < n; ++j) {
+    const kvs::LookupOut &d = st.h<kvs::LookupOut>(out_off)[j];
+    const uint32_t i = ord.perm[j];
+    const bool dev_hit = d.status != kvs::kMiss;
+    const bool host_hit = host_slot[i] != kvs::kBucketEmpty;
+    if (dev_hit != host_hit || (dev_hit && (d.slot != host_slot[i] || d.status != res[i].status))) {
+      c->quarantined = true;
+      return set_err(KVS_E_CUDA, "get_blocks: device index replica disagrees with the catalog for key %u", i);
     }
   }
   TRY(end_op(c, stream));
