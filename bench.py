@@ -76,6 +76,8 @@ def parse() -> argparse.Namespace:
                     help="sharded store: P2P stores over NVLink (default) or NCCL send/recv of packed values")
     ap.add_argument("--mix", action="store_true",
                     help="hash-sharded 70/30 get/put mix of 256-block batches, config-1 KV shape, both transports")
+    ap.add_argument("--fill", action="store_true",
+                    help="token-granular paged fill: 8192 tokens of 4 requests into 64 layers' caches")
     ap.add_argument("--resident", type=int, default=0,
                     help="--mix: resident blocks per GPU (default: 1M / N, at most 16384: the pinned host "
                          "tier mirrors every resident block)")
@@ -986,10 +988,74 @@ def run_multiturn(args):
             "pcie_bytes": {"h2d_admissions": sst["admissions"] * vlen, "d2h_write_through": sst["writes_through"] * vlen}}
 
 
+def run_fill(args):
+    """moreh_paged_fill_cache_varlen on B200: per layer, 8192 packed tokens of 4 requests (chunked-
+    prefill start positions) into a paged bf16 cache of 64-token blocks, 8 KV heads x 128; the 64
+    layers use distinct inputs and caches (4 GiB of fill, more than L2). Kernel time from CUDA
+    events around each launch; algorithmic bytes = read + write of every filled row."""
+    import torch
+
+    from kvcache_manager import ops
+
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(11)
+    lens, starts, bs = [3072, 2048, 1024, 2048], [0, 512, 4096, 64], 64
+    max_blocks = max((s0 + n + bs - 1) // bs for s0, n in zip(starts, lens))
+    nb = 4 * max_blocks + 1
+    pt = torch.from_numpy(rng.permutation(np.arange(1, nb))[: 4 * max_blocks].reshape(4, max_blocks).astype(np.int32)).cuda()
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device="cuda")
+    sp = torch.tensor(starts, dtype=torch.int32, device="cuda")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    layers = 8 if args.small else 64
+    fills = [[torch.empty((1, HEADS, 8192, HEAD_DIM), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+              for _ in range(2)] for _ in range(layers)]
+    caches = [[torch.zeros((nb, HEADS, bs, HEAD_DIM), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+              for _ in range(layers)]
+    for _ in range(args.warmup):
+        for (kf, vf), (ck, cv) in zip(fills, caches):
+            ops.paged_fill_cache_varlen(kf, vf, cu, pt, sp, ck, cv)
+    torch.cuda.synchronize()
+    times = []
+    stream = torch.cuda.current_stream()
+    for _ in range(args.steps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
+        # hold the stream while the host queues every layer, so each event pair brackets the
+        # kernel alone and not the host's argument checks
+        torch.cuda._sleep(50_000_000)
+        for ((kf, vf), (ck, cv)), (e0, e1) in zip(zip(fills, caches), ev):
+            e0.record(stream)
+            ops.paged_fill_cache_varlen(kf, vf, cu, pt, sp, ck, cv)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        times += [e0.elapsed_time(e1) for e0, e1 in ev]
+    # check one layer against a plain torch restatement of the fill
+    kf, ck = fills[7][0], caches[7][0]
+    tok = 0
+    for r, (n, s0) in enumerate(zip(lens, starts)):
+        pos = torch.arange(s0, s0 + n, device="cuda")
+        blk = pt[r][pos // bs].long()
+        want = kf[0, :, tok:tok + n].permute(1, 0, 2)
+        if not torch.equal(ck[blk, :, pos % bs], want):
+            raise RuntimeError("paged fill differs from the torch restatement")
+        tok += n
+    row = HEAD_DIM * 2
+    bytes_per_launch = 2 * 2 * HEADS * sum(lens) * row  # K and V, read + write
+    avg_ms = statistics.mean(times)
+    achieved = bytes_per_launch / (avg_ms / 1e3) / GB
+    peak, kind = measured_peaks()
+    return {"fill": "moreh_paged_fill_cache_varlen restated token-granular: 8192 tokens, 4 requests, 8 KV heads x 128 "
+                    f"bf16, 64-token blocks, {layers} layers (distinct inputs)",
+            "launches": len(times), "avg_launch_ms": round(avg_ms, 4), "algorithmic_bytes_per_launch": bytes_per_launch,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind,
+                         "frac": round(achieved / peak, 4), "unit": "GB/s"},
+            "restore_64_layers_ms": round(avg_ms * layers, 3)}
+
+
 def main():
     args = parse()
-    if args.sweep or args.multiturn:
-        print(json.dumps(run_sweep(args) if args.sweep else run_multiturn(args)))
+    if args.sweep or args.multiturn or args.fill:
+        print(json.dumps(run_sweep(args) if args.sweep else run_multiturn(args) if args.multiturn else run_fill(args)))
         return
     rank, local_rank, world = dist_env()
     if args.mix and world == 1:

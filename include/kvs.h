@@ -255,6 +255,25 @@ int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, c
 int kvs_copy_values(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *addrs, int to_rows,
                     void *stream);
 
+/* ---- token-granular paged KV fill ----
+ * Replaces ttnn.experimental.moreh_paged_fill_cache_varlen (patch 0002 lines 106-421: reader /
+ * writer kernels, validation at lines 441-545). k_fill / v_fill: [n_heads][total_tokens] rows of
+ * row_bytes (one [1, H, T, D] tensor each); cache_k / cache_v: [num_blocks][n_heads][block_size]
+ * rows; cu_seqlens: batch + 1 int32 offsets, padded with -1 after the valid ones; page_table:
+ * [batch][max_blocks_per_seq] int32; start_positions: [batch] int32. Token t below the valid total
+ * of request r (the last i with cu_seqlens[i] <= t) goes to cache position
+ * p = t - cu_seqlens[r] + start_positions[r]: block page_table[r][p / block_size], row
+ * p % block_size, every head. Entries <= 0 skip the token (vLLM's null block 0, -1 for unused
+ * slots) as in the reference. The reference moves 32-token tiles; this fill moves single tokens
+ * and equals it whenever boundaries, start positions and block_size are multiples of 32. A
+ * position beyond the page-table row or a block >= num_blocks (the reference would read or write
+ * out of bounds) skips the token and increments *out_of_range when given (a device word).
+ * All arrays are device memory of one GPU; asynchronous on `stream`. */
+int kvs_paged_fill_varlen(const void *k_fill, const void *v_fill, uint32_t n_heads, uint32_t total_tokens,
+                          uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
+                          uint32_t max_blocks_per_seq, const int32_t *start_positions, void *cache_k, void *cache_v,
+                          uint32_t num_blocks, uint32_t block_size, uint32_t *out_of_range, void *stream);
+
 /* ---- chunk gather / scatter ops ----
  * gather_tp_shards_to_chip / pack_local_shards (patch 0003 gather.hpp lines 9372-9417) and
  * their inverses scatter_chunk_from_chip / unpack_local_shards (9418-9453).

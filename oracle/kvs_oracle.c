@@ -1314,3 +1314,55 @@ int kvo_get_blocks(kvo_store *s, uint8_t *const *members, uint32_t n_members, ui
   free_fmt(&f);
   return rc;
 }
+
+/* --- token-granular paged KV fill: reader_fill_cache_varlen.cpp / writer_fill_cache_varlen.cpp
+ * (patch 0002). The valid total is found as the reader does (the last cu entry that is not -1,
+ * by bisection over [0, batch]); a token's request as the writer's find_request_idx does (the last
+ * i in [0, batch] with cu[i] <= t, unsigned, so -1 padding never matches). --- */
+static uint32_t fill_valid_total(const int32_t *cu, uint32_t batch) {
+  uint32_t lo = 0, hi = batch;
+  while (lo < hi) {
+    uint32_t mid = (lo + hi + 1) >> 1;
+    if ((uint32_t)cu[mid] != 0xFFFFFFFFu) lo = mid; else hi = mid - 1;
+  }
+  return (uint32_t)cu[lo];
+}
+
+static uint32_t fill_request_of(const int32_t *cu, uint32_t batch, uint32_t t) {
+  uint32_t lo = 0, hi = batch;
+  while (lo < hi) {
+    uint32_t mid = (lo + hi + 1) >> 1;
+    if ((uint32_t)cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+int kvo_paged_fill_varlen(const uint8_t *k_fill, const uint8_t *v_fill, uint32_t n_heads, uint32_t total_tokens,
+                          uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
+                          uint32_t max_blocks_per_seq, const int32_t *start_positions, uint8_t *cache_k,
+                          uint8_t *cache_v, uint32_t num_blocks, uint32_t block_size, uint64_t *out_of_range) {
+  if (!k_fill || !v_fill || !cu_seqlens || !page_table || !start_positions || !cache_k || !cache_v || batch == 0 ||
+      block_size == 0 || row_bytes == 0)
+    return fail(KVO_E_INVAL, "paged_fill_varlen: invalid arguments");
+  uint64_t oor = 0;
+  uint32_t limit = fill_valid_total(cu_seqlens, batch);
+  if (limit > total_tokens) limit = total_tokens;
+  for (uint32_t t = 0; t < limit; ++t) {
+    const uint32_t r = fill_request_of(cu_seqlens, batch, t);
+    if (r >= batch) { ++oor; continue; }
+    const uint32_t pos = t - (uint32_t)cu_seqlens[r] + (uint32_t)start_positions[r];
+    const uint32_t vb = pos / block_size;
+    if (vb >= max_blocks_per_seq) { ++oor; continue; }
+    const int32_t phys = page_table[(uint64_t)r * max_blocks_per_seq + vb];
+    if (phys <= 0) continue; /* null block or an unused / padded slot */
+    if ((uint32_t)phys >= num_blocks) { ++oor; continue; }
+    for (uint32_t h = 0; h < n_heads; ++h) {
+      const uint64_t src = ((uint64_t)h * total_tokens + t) * row_bytes;
+      const uint64_t dst = (((uint64_t)phys * n_heads + h) * block_size + pos % block_size) * row_bytes;
+      memcpy(cache_k + dst, k_fill + src, row_bytes);
+      memcpy(cache_v + dst, v_fill + src, row_bytes);
+    }
+  }
+  if (out_of_range) *out_of_range = oor;
+  return KVO_OK;
+}

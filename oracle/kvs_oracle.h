@@ -197,6 +197,24 @@ int kvo_get_blocks(kvo_store *s, uint8_t *const *members, uint32_t n_members, ui
                    const uint64_t *member_bytes, const uint64_t *keys, const uint32_t *block_ids,
                    uint32_t n, uint8_t *found, int n_threads);
 
+/* ---- token-granular paged KV fill (moreh_paged_fill_cache_varlen) ----
+ * Restates the reader / writer kernels of moreh_paged_fill_cache_varlen (patch 0002,
+ * reader_fill_cache_varlen.cpp and writer_fill_cache_varlen.cpp) one token at a time on row-major
+ * buffers. k_fill / v_fill: [n_heads][total_tokens] rows of row_bytes; caches:
+ * [num_blocks][n_heads][block_size] rows. cu_seqlens: batch + 1 offsets, padded with -1; the
+ * valid total is the last entry before the padding. Token t (below that total and below
+ * total_tokens) of request r = the last i with (uint32)cu[i] <= t goes to cache position
+ * pos = t - cu[r] + start_positions[r], block page_table[r][pos / block_size], row pos % block_size,
+ * for every head; a page-table entry of 0 (vLLM's null block) or below 0 skips the token. The
+ * reference moves 32-token tiles, so both agree whenever request boundaries, start positions and
+ * the block size are multiples of 32. Tokens whose position lies beyond the page-table row or whose
+ * block is >= num_blocks (the reference would read or write out of bounds) are skipped and
+ * counted in *out_of_range. */
+int kvo_paged_fill_varlen(const uint8_t *k_fill, const uint8_t *v_fill, uint32_t n_heads, uint32_t total_tokens,
+                          uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
+                          uint32_t max_blocks_per_seq, const int32_t *start_positions, uint8_t *cache_k,
+                          uint8_t *cache_v, uint32_t num_blocks, uint32_t block_size, uint64_t *out_of_range);
+
 #ifdef __cplusplus
 }
 #endif

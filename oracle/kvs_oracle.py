@@ -113,6 +113,7 @@ def lib():
             "kvo_block_format": (u64, [u32, u32, P, P, u32, P, P]),
             "kvo_put_blocks": (C.c_int, [P, P, u32, u32, P, P, P, u32, C.c_int]),
             "kvo_get_blocks": (C.c_int, [P, P, u32, u32, P, P, P, u32, P, C.c_int]),
+            "kvo_paged_fill_varlen": (C.c_int, [P, P, u32, u32, u32, P, u32, P, u32, P, P, P, u32, u32, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -367,3 +368,24 @@ def block_format(member_bytes, members_per_layer=2):
     if not vlen:
         raise OracleError("members must be whole layers")
     return words[: nw.value].copy(), rb, int(vlen)
+
+
+def paged_fill_varlen(k_fill, v_fill, cu_seqlens, page_table, start_positions, cache_k, cache_v):
+    """Token-granular moreh_paged_fill_cache_varlen on numpy arrays, caches updated in place.
+
+    k_fill / v_fill: (heads, total_tokens, head_dim) of any dtype; caches: (num_blocks, heads,
+    block_size, head_dim) of the same dtype; cu_seqlens (batch + 1,), page_table (batch,
+    max_blocks_per_seq) and start_positions (batch,) int32. Returns the out-of-range token count."""
+    heads, total, dim = k_fill.shape
+    nb, h2, bs, d2 = cache_k.shape
+    assert (h2, d2) == (heads, dim) and v_fill.shape == k_fill.shape and cache_v.shape == cache_k.shape
+    for a in (k_fill, v_fill, cache_k, cache_v):
+        assert a.flags.c_contiguous and a.dtype == k_fill.dtype
+    cu = np.ascontiguousarray(cu_seqlens, np.int32)
+    pt = np.ascontiguousarray(page_table, np.int32)
+    sp = np.ascontiguousarray(start_positions, np.int32)
+    oor = C.c_uint64()
+    _check(lib().kvo_paged_fill_varlen(_ptr(k_fill), _ptr(v_fill), heads, total, dim * k_fill.itemsize, _ptr(cu),
+                                       pt.shape[0], _ptr(pt), pt.shape[1], _ptr(sp), _ptr(cache_k), _ptr(cache_v),
+                                       nb, bs, C.addressof(oor)))
+    return int(oor.value)

@@ -458,6 +458,184 @@ int copy_ctas_per_sm() {
   return per_sm;
 }
 
+// ---------------------------------------------------------------- token-granular paged fill
+//
+// One CTA per (32-token chunk, group of heads); the grid has about two CTAs per SM. Every warp
+// resolves the chunk's 32 destinations itself, lane i for token i (last cu_seqlens entry <= token, unsigned so the -1 padding never
+// matches; then page_table[request][pos / block_size]), and hands them around with shuffles, so
+// no block barrier separates the lookups from the copy (issuing the first round of source loads
+// ahead of the lookups measured 11 % slower on B200). The
+// chunk's source rows are contiguous in the packed input; rows move as 16-byte streaming loads
+// and stores over one flattened (head, K|V, token, word) index. Skips: tokens at or past the
+// valid total (the last cu entry before the -1 padding), page-table entries <= 0 (vLLM's null
+// block, unused slots), and positions or blocks out of range (counted in p.out_of_range instead
+// of being written out of bounds).
+
+constexpr int kFillTokens = 32;
+constexpr int kFillThreads = 256;
+
+__device__ __forceinline__ uint32_t fill_valid_total(const int32_t *cu, uint32_t batch) {
+  uint32_t lo = 0, hi = batch;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi + 1) >> 1;
+    if ((uint32_t)__ldg(cu + mid) != 0xFFFFFFFFu) lo = mid; else hi = mid - 1;
+  }
+  return (uint32_t)__ldg(cu + lo);
+}
+
+// Cache row (for head 0) of token t, or -1 to skip it; *oor marks an out-of-range skip.
+__device__ __forceinline__ long long fill_row_of(const PagedFillParams &p, uint32_t t, bool *oor) {
+  uint32_t lo = 0, hi = p.batch;  // request of token t
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi + 1) >> 1;
+    if ((uint32_t)__ldg(p.cu_seqlens + mid) <= t) lo = mid; else hi = mid - 1;
+  }
+  *oor = false;
+  if (lo >= p.batch) {
+    *oor = true;
+    return -1;
+  }
+  const uint32_t pos = t - (uint32_t)__ldg(p.cu_seqlens + lo) + (uint32_t)__ldg(p.start_positions + lo);
+  const uint32_t vb = pos / p.block_size;
+  if (vb >= p.max_blocks) {
+    *oor = true;
+    return -1;
+  }
+  const int32_t phys = __ldg(p.page_table + (uint64_t)lo * p.max_blocks + vb);
+  if (phys <= 0) return -1;
+  if ((uint32_t)phys >= p.num_blocks) {
+    *oor = true;
+    return -1;
+  }
+  return (long long)phys * p.n_heads * p.block_size + pos % p.block_size;
+}
+
+// The same lookup for batches of fewer than 32 requests, from registers: lane j holds
+// cu_seqlens[j] and start_positions[j] (one parallel load per warp), the valid total is the last
+// lane whose entry is not -1, and a token's request is found by binary lifting over shuffles
+// (cu_seqlens is non-decreasing up to the -1 padding, which compares as the largest value).
+__device__ __forceinline__ long long fill_row_small(const PagedFillParams &p, uint32_t cu_l, uint32_t sp_l,
+                                                    uint32_t t, bool want, bool *oor) {
+  uint32_t r = 0;
+#pragma unroll
+  for (uint32_t step = 16; step >= 1; step >>= 1) {
+    const uint32_t cand = r + step;
+    const uint32_t v = __shfl_sync(0xFFFFFFFFu, cu_l, cand < 32 ? cand : 31);
+    if (cand <= p.batch && v <= t) r = cand;
+  }
+  const uint32_t cu_r = __shfl_sync(0xFFFFFFFFu, cu_l, r);
+  const uint32_t sp_r = __shfl_sync(0xFFFFFFFFu, sp_l, r);
+  *oor = false;
+  if (!want) return -1;
+  if (r >= p.batch) {
+    *oor = true;
+    return -1;
+  }
+  const uint32_t pos = t - cu_r + sp_r;
+  const uint32_t vb = pos / p.block_size;
+  if (vb >= p.max_blocks) {
+    *oor = true;
+    return -1;
+  }
+  const int32_t phys = __ldg(p.page_table + (uint64_t)r * p.max_blocks + vb);
+  if (phys <= 0) return -1;
+  if ((uint32_t)phys >= p.num_blocks) {
+    *oor = true;
+    return -1;
+  }
+  return (long long)phys * p.n_heads * p.block_size + pos % p.block_size;
+}
+
+constexpr int kFillUnroll = 4;  // 16-byte words in flight per thread per round
+
+__global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFillParams p) {
+  const uint32_t t0 = blockIdx.x * kFillTokens;
+  const uint32_t heads_per = (p.n_heads + gridDim.y - 1) / gridDim.y;
+  const uint32_t h0 = blockIdx.y * heads_per;
+  const uint32_t h1 = min(p.n_heads, h0 + heads_per);
+  const uint32_t lane = threadIdx.x & 31;
+  const bool small = p.batch < 32;
+  uint32_t cu_l = 0xFFFFFFFFu, sp_l = 0;
+  uint32_t limit;
+  if (small) {
+    if (lane <= p.batch) cu_l = (uint32_t)__ldg(p.cu_seqlens + lane);
+    if (lane < p.batch) sp_l = (uint32_t)__ldg(p.start_positions + lane);
+    const uint32_t valid = __ballot_sync(0xFFFFFFFFu, lane <= p.batch && cu_l != 0xFFFFFFFFu);
+    limit = valid ? __shfl_sync(0xFFFFFFFFu, cu_l, 31 - __clz(valid)) : 0u;
+  } else {
+    limit = fill_valid_total(p.cu_seqlens, p.batch);
+  }
+  if (limit > p.total_tokens) limit = p.total_tokens;
+  if (h0 >= h1 || t0 >= limit) return;  // uniform across the CTA
+  const uint32_t nt = min((uint32_t)kFillTokens, limit - t0);
+  const uint64_t rb = p.row_bytes;
+  const bool vec = ((reinterpret_cast<uint64_t>(p.k_fill) | reinterpret_cast<uint64_t>(p.v_fill) |
+                     reinterpret_cast<uint64_t>(p.cache_k) | reinterpret_cast<uint64_t>(p.cache_v) | rb) & 15u) == 0;
+  if (vec) {
+    const uint32_t wpr = (uint32_t)(rb >> 4);  // 16-byte words per row
+    const uint32_t per_side = nt * wpr;
+    const uint32_t total = (h1 - h0) * 2 * per_side;
+    // word i of the flattened (head, K|V, token, word) index: its source, its token
+    auto src_of = [&](uint32_t i, uint32_t *tok, uint32_t *h, uint32_t *side, uint32_t *in_side) {
+      const uint32_t hs = i / per_side;
+      *in_side = i - hs * per_side;
+      *tok = *in_side / wpr;
+      *h = h0 + (hs >> 1);
+      *side = hs & 1;
+      const uint8_t *src = (*side ? p.v_fill : p.k_fill) + ((uint64_t)*h * p.total_tokens + t0) * rb;
+      return reinterpret_cast<const int4 *>(src) + *in_side;
+    };
+    int4 v[kFillUnroll];
+    bool oor = false;
+    const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor)
+                                   : (lane < nt ? fill_row_of(p, t0 + lane, &oor) : -1);
+    if (oor && threadIdx.x < 32 && blockIdx.y == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
+    // warp-uniform trip count (every lane joins the shuffles): run while the warp's lane 0 is in range
+    for (uint32_t base = threadIdx.x; base - lane < total; base += kFillThreads * kFillUnroll) {
+      uint64_t dst[kFillUnroll];
+#pragma unroll
+      for (int u = 0; u < kFillUnroll; ++u) {
+        const uint32_t i = base + u * kFillThreads;
+        const bool live = i < total;
+        uint32_t tok = 0, h = 0, side = 0, in_side = 0;
+        const int4 *src = live ? src_of(i, &tok, &h, &side, &in_side) : nullptr;
+        if (live) v[u] = ld_stream(src);  // in bounds whether or not the token is written
+        const long long row = __shfl_sync(0xFFFFFFFFu, my_row, tok);
+        dst[u] = 0;
+        if (live && row >= 0) {
+          uint8_t *cache = side ? p.cache_v : p.cache_k;
+          dst[u] = reinterpret_cast<uint64_t>(cache + ((uint64_t)row + (uint64_t)h * p.block_size) * rb) +
+                   (uint64_t)(in_side - tok * wpr) * 16u;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kFillUnroll; ++u)
+        if (dst[u]) st_stream(reinterpret_cast<int4 *>(dst[u]), v[u]);
+    }
+  } else {
+    bool oor = false;
+    const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor)
+                                   : (lane < nt ? fill_row_of(p, t0 + lane, &oor) : -1);
+    if (oor && threadIdx.x < 32 && blockIdx.y == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
+    const uint64_t per_side = (uint64_t)nt * rb;
+    const uint64_t total = (uint64_t)(h1 - h0) * 2 * per_side;
+    for (uint64_t base = threadIdx.x; base - lane < total; base += kFillThreads) {
+      const uint64_t i = base;
+      const bool live = i < total;
+      const uint64_t hs = live ? i / per_side : 0;
+      const uint64_t in_side = live ? i - hs * per_side : 0;
+      const uint32_t tok = (uint32_t)(in_side / rb);
+      const long long row = __shfl_sync(0xFFFFFFFFu, my_row, tok);
+      if (live && row >= 0) {
+        const uint32_t h = h0 + (uint32_t)(hs >> 1), side = (uint32_t)(hs & 1);
+        const uint8_t *src = (side ? p.v_fill : p.k_fill) + ((uint64_t)h * p.total_tokens + t0) * rb;
+        uint8_t *cache = side ? p.cache_v : p.cache_k;
+        cache[((uint64_t)row + (uint64_t)h * p.block_size) * rb + (in_side - (uint64_t)tok * rb)] = src[in_side];
+      }
+    }
+  }
+}
+
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas) {
   if (p.total_tiles == 0 && (p.n_header_words == 0 || !p.to_blob)) return cudaSuccess;
   uint64_t grid = grid_ctas > 0 ? (uint64_t)grid_ctas : (uint64_t)sm_count() * copy_ctas_per_sm();
@@ -507,6 +685,21 @@ cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream)
   uint64_t grid = (work + 255) / 256;
   if (grid > 1024) grid = 1024;
   apply_mutations_kernel<<<(unsigned)grid, 256, 0, stream>>>(p);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_fill(const PagedFillParams &p, cudaStream_t stream) {
+  if (p.total_tokens == 0 || p.n_heads == 0) return cudaSuccess;
+  // split the heads into groups only as far as needed for about two CTAs per SM
+  const uint32_t chunks = (p.total_tokens + kFillTokens - 1) / kFillTokens;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  uint32_t groups = (2u * (uint32_t)sms + chunks - 1) / chunks;
+  groups = groups < 1 ? 1 : (groups > p.n_heads ? p.n_heads : groups);
+  const dim3 grid(chunks, groups);
+  paged_fill_kernel<<<grid, kFillThreads, 0, stream>>>(p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }

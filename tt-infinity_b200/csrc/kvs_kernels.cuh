@@ -1,6 +1,6 @@
 // kvs_kernels.cuh -- device-side data structures and kernel launchers of the B200 KV block store.
 //
-// Three kernel families move every byte and answer every device-side lookup:
+// Four kernel families move every byte and answer every device-side lookup:
 //   * chunk_copy: the paged-block gather (put) / scatter (get) engine. It moves whole member
 //     blocks between paged KV tensors and packed blobs (device slab values or caller blobs),
 //     16-byte vectorised and coalesced, tiles spread over a persistent grid of 148 x k CTAs.
@@ -11,6 +11,8 @@
 //     for empty / hash-matching lanes, and a 32-lane key compare against the directory row.
 //   * apply_mutations: brings the device index replica up to date with the host directory
 //     (bucket words, entry metadata, key rows) in stream order before any lookup reads it.
+//   * paged_fill: token-granular fill of packed K/V rows of several requests into a paged cache
+//     through page tables (moreh_paged_fill_cache_varlen, patch 0002 lines 106-421).
 #pragma once
 
 #include <cstdint>
@@ -100,6 +102,18 @@ struct MutationParams {
   uint32_t *key_rows;
 };
 
+// Token-granular paged KV fill (moreh_paged_fill_cache_varlen): packed K/V rows of several
+// requests into their paged cache blocks through page tables. All arrays are device memory.
+struct PagedFillParams {
+  const uint8_t *k_fill, *v_fill;    // [n_heads][total_tokens][row_bytes]
+  uint8_t *cache_k, *cache_v;        // [num_blocks][n_heads][block_size][row_bytes]
+  const int32_t *cu_seqlens;         // [batch + 1], -1 padded
+  const int32_t *page_table;         // [batch][max_blocks]
+  const int32_t *start_positions;    // [batch]
+  uint32_t n_heads, total_tokens, row_bytes, batch, max_blocks, num_blocks, block_size;
+  unsigned int *out_of_range;        // optional: tokens skipped for a position or block out of range
+};
+
 // Launch helpers (return cudaError_t of the launch). `grid_ctas` = 0 picks the default
 // persistent grid (SM count x resident CTAs per SM).
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas = 0);
@@ -109,6 +123,7 @@ cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream)
 cudaError_t read_tma_timeouts(unsigned int *count);
 cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream);
 cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream);
+cudaError_t launch_paged_fill(const PagedFillParams &p, cudaStream_t stream);
 cudaError_t launch_echo(const uint8_t *in, uint8_t *out, uint32_t n, cudaStream_t stream);
 
 // Host-side FNV-1a 32 (the same function the device probe computes).

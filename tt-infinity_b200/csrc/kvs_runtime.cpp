@@ -2456,6 +2456,51 @@ static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_me
   return KVS_OK;
 }
 
+int kvs_paged_fill_varlen(const void *k_fill, const void *v_fill, uint32_t n_heads, uint32_t total_tokens,
+                          uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
+                          uint32_t max_blocks_per_seq, const int32_t *start_positions, void *cache_k, void *cache_v,
+                          uint32_t num_blocks, uint32_t block_size, uint32_t *out_of_range, void *stream) {
+  const char *op = "paged_fill_varlen";
+  if (batch == 0) return set_err(KVS_E_INVAL, "%s: page_table must have at least one row", op);
+  if (block_size == 0 || row_bytes == 0 || n_heads == 0)
+    return set_err(KVS_E_INVAL, "%s: block_size, head row bytes and num_kv_heads must be > 0", op);
+  if (max_blocks_per_seq > num_blocks)
+    return set_err(KVS_E_INVAL, "%s: max_num_blocks_per_seq (%u) must be <= max_num_blocks (%u)", op,
+                   max_blocks_per_seq, num_blocks);
+  const void *ptrs[] = {k_fill, v_fill, cu_seqlens, page_table, start_positions, cache_k, cache_v};
+  const char *names[] = {"k_fill_value", "v_fill_value", "cu_seqlens", "page_table", "start_positions", "cache_k",
+                         "cache_v"};
+  int device = -1;
+  for (int i = 0; i < 7; ++i) {
+    cudaPointerAttributes a{};
+    if (!ptrs[i] || cudaPointerGetAttributes(&a, ptrs[i]) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+      cudaGetLastError();
+      return set_err(KVS_E_INVAL, "%s: %s must be on device!", op, names[i]);
+    }
+    if (device < 0) device = a.device;
+    if (a.device != device) return set_err(KVS_E_INVAL, "%s: All tensors must be on the same device!", op);
+  }
+  DeviceGuard g(device);
+  kvs::PagedFillParams p{};
+  p.k_fill = static_cast<const uint8_t *>(k_fill);
+  p.v_fill = static_cast<const uint8_t *>(v_fill);
+  p.cache_k = static_cast<uint8_t *>(cache_k);
+  p.cache_v = static_cast<uint8_t *>(cache_v);
+  p.cu_seqlens = cu_seqlens;
+  p.page_table = page_table;
+  p.start_positions = start_positions;
+  p.n_heads = n_heads;
+  p.total_tokens = total_tokens;
+  p.row_bytes = row_bytes;
+  p.batch = batch;
+  p.max_blocks = max_blocks_per_seq;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.out_of_range = out_of_range;
+  CUDA_TRY(kvs::launch_paged_fill(p, static_cast<cudaStream_t>(stream)));
+  return KVS_OK;
+}
+
 int kvs_gather_chunk(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_members,
                      const uint64_t *member_block_bytes, const uint64_t *member_extent, const uint32_t *block_ids,
                      uint32_t n_blocks, const uint64_t *region_bases, const uint32_t *header_words,

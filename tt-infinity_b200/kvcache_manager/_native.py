@@ -200,6 +200,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvs_puts_landed": (C.c_int, [P, P]),
     "kvs_copy_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, _i64p, _u64p, C.c_int, P]),
     "kvs_copy_values": (C.c_int, [P, P, C.c_uint64, C.c_uint32, _u64p, C.c_int, P]),
+    "kvs_paged_fill_varlen": (
+        C.c_int,
+        [P, P, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint32, P, C.c_uint32, P, P, P, C.c_uint32, C.c_uint32, P, P],
+    ),
     "kvs_client_set_timing": (C.c_int, [P, C.c_int]),
     "kvs_client_timing": (C.c_int, [P, C.POINTER(KernelTiming), C.POINTER(KernelTiming)]),
     "kvs_gather_chunk": (

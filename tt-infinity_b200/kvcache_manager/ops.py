@@ -1,4 +1,5 @@
-"""Chunk gather / scatter ops over paged KV members (torch CUDA tensors).
+"""Chunk gather / scatter ops over paged KV members, and the token-granular paged fill (torch
+CUDA tensors).
 
 B200 counterparts of ttnn.kvcache_manager.gather_tp_shards_to_chip / scatter_chunk_from_chip /
 pack_local_shards / unpack_local_shards (patch 0003 gather.hpp lines 9335-9453). A "rank" is a
@@ -106,3 +107,72 @@ def unpack_local_shards(src: Any, members: Sequence[Any], block_ids: Sequence[in
 
 __all__ = ["gather_tp_shards_to_chip", "scatter_chunk_from_chip", "pack_local_shards", "unpack_local_shards"]
 _ = _native
+
+
+def paged_fill_cache_varlen(k_fill_value: Any, v_fill_value: Any, cu_seqlens: Any, page_table: Any,
+                            start_positions: Any, cache_k: Any, cache_v: Any, out_of_range: Any = None):
+    """Fill packed K/V of several requests into a paged KV cache, one token at a time.
+
+    The B200 counterpart of ttnn.experimental.moreh_paged_fill_cache_varlen (patch 0002: kernels at
+    lines 106-421, validation at 441-545), with its argument order and checks:
+    k_fill_value / v_fill_value [1, num_kv_heads, total_tokens, head_dim]; cache_k / cache_v
+    [max_num_blocks, num_kv_heads, block_size, head_dim] of the same dtype; cu_seqlens int32
+    [batch_size + 1] (-1 after the valid offsets); page_table int32 [batch_size,
+    max_num_blocks_per_seq]; start_positions int32 [batch_size]; every tensor a contiguous CUDA
+    tensor on one device. Page-table entries <= 0 skip a token (vLLM's null block 0, -1 for unused
+    slots). out_of_range: optional int32 CUDA tensor of one element, incremented for tokens skipped
+    because their position or block is out of range. Asynchronous on the current stream; returns
+    (cache_k, cache_v) as the reference's device operation does."""
+    torch = _torch()
+    ts = {"k_fill_value": k_fill_value, "v_fill_value": v_fill_value, "cu_seqlens": cu_seqlens,
+          "page_table": page_table, "start_positions": start_positions, "cache_k": cache_k, "cache_v": cache_v}
+    for name, t in ts.items():
+        if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+            raise RuntimeError(f"{name} must be on device!")
+        if not t.is_contiguous():
+            raise RuntimeError(f"{name} must be contiguous")
+    dev = k_fill_value.device
+    if any(t.device != dev for t in ts.values()):
+        raise RuntimeError("All tensors must be on the same device!")
+    if k_fill_value.dtype != cache_k.dtype:
+        raise RuntimeError(f"k_fill_value dtype ({k_fill_value.dtype}) must match cache_k dtype ({cache_k.dtype})")
+    if v_fill_value.dtype != cache_v.dtype:
+        raise RuntimeError(f"v_fill_value dtype ({v_fill_value.dtype}) must match cache_v dtype ({cache_v.dtype})")
+    if k_fill_value.dim() != 4 or cache_k.dim() != 4:
+        raise RuntimeError("k_fill_value and cache_k must be 4-D")
+    if k_fill_value.shape[0] != 1:
+        raise RuntimeError(f"k_fill_value first dim must be 1, got {k_fill_value.shape[0]}")
+    if v_fill_value.shape[0] != 1:
+        raise RuntimeError(f"v_fill_value first dim must be 1, got {v_fill_value.shape[0]}")
+    if k_fill_value.shape[-1] != cache_k.shape[-1]:
+        raise RuntimeError("head_dim of k_fill_value must match cache_k")
+    if v_fill_value.shape[-1] != cache_v.shape[-1]:
+        raise RuntimeError("head_dim of v_fill_value must match cache_v")
+    if k_fill_value.shape != v_fill_value.shape:
+        raise RuntimeError("k_fill_value and v_fill_value must have the same shape")
+    if cache_k.shape != cache_v.shape:
+        raise RuntimeError("cache_k and cache_v must have the same shape")
+    if k_fill_value.shape[1] != cache_k.shape[1]:
+        raise RuntimeError("num_kv_heads of k_fill_value must match cache_k")
+    for name in ("cu_seqlens", "page_table", "start_positions"):
+        if ts[name].dtype != torch.int32:
+            raise RuntimeError(f"{name} must be INT32")
+    if page_table.dim() != 2:
+        raise RuntimeError("page_table must be [batch_size, max_num_blocks_per_seq]")
+    if page_table.shape[1] > cache_k.shape[0]:
+        raise RuntimeError(f"max_num_blocks_per_seq ({page_table.shape[1]}) must be <= max_num_blocks ({cache_k.shape[0]})")
+    if start_positions.shape[0] != page_table.shape[0]:
+        raise RuntimeError(f"start_positions size ({start_positions.shape[0]}) must match batch_size ({page_table.shape[0]})")
+    if cu_seqlens.numel() != page_table.shape[0] + 1:
+        raise RuntimeError(f"cu_seqlens must hold batch_size + 1 = {page_table.shape[0] + 1} entries")
+    if out_of_range is not None and (out_of_range.dtype != torch.int32 or out_of_range.device != dev):
+        raise RuntimeError("out_of_range must be an int32 tensor on the fill's device")
+    heads, total, dim = k_fill_value.shape[1], k_fill_value.shape[2], k_fill_value.shape[3]
+    P = C.c_void_p
+    check(load().kvs_paged_fill_varlen(
+        P(k_fill_value.data_ptr()), P(v_fill_value.data_ptr()), heads, total, dim * k_fill_value.element_size(),
+        P(cu_seqlens.data_ptr()), page_table.shape[0], P(page_table.data_ptr()), page_table.shape[1],
+        P(start_positions.data_ptr()), P(cache_k.data_ptr()), P(cache_v.data_ptr()), cache_k.shape[0],
+        cache_k.shape[2], P(out_of_range.data_ptr() if out_of_range is not None else None),
+        P(torch.cuda.current_stream(dev).cuda_stream)))
+    return cache_k, cache_v
