@@ -247,7 +247,9 @@ int kvs_puts_landed(kvs_client *c, void *stream);
 
 /* Client side: one copy launch between the layout's blocks (this GPU's memory) and explicit
  * value addresses (this GPU's or a peer's); to_blob 1 gathers (writes the value header too),
- * 0 scatters. Addresses are 16-byte aligned; a zero address skips the block. */
+ * 0 scatters. Addresses are 16-byte aligned; a zero address skips the block. When every address
+ * lies in a shard's slab or a mapping opened by kvs_ipc_open the bulk-copy engine moves the
+ * bytes, otherwise plain 16-byte loads and stores (any memory the GPU can address). */
 int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const int64_t *block_ids,
                     const uint64_t *blob_addrs, int to_blob, void *stream);
 /* One copy launch between whole values at explicit addresses and contiguous rows:

@@ -63,6 +63,34 @@ int set_err(int code, const char *fmt, ...) {
     if (rc_ != KVS_OK) return rc_; \
   } while (0)
 
+// Device allocations the runtime knows: every shard's slab and every peer mapping opened from an
+// IPC handle. A copy whose blob addresses all fall inside them may use the bulk-copy engine, which
+// needs device memory on both sides (this GPU's or a peer's).
+std::mutex g_ranges_mu;
+std::map<uint64_t, uint64_t> g_ranges;  // base -> bytes
+
+void dev_range_add(const void *base, uint64_t bytes) {
+  std::lock_guard<std::mutex> lk(g_ranges_mu);
+  g_ranges[reinterpret_cast<uint64_t>(base)] = bytes;
+}
+
+void dev_range_remove(const void *base) {
+  std::lock_guard<std::mutex> lk(g_ranges_mu);
+  g_ranges.erase(reinterpret_cast<uint64_t>(base));
+}
+
+bool dev_ranges_hold(const uint64_t *addrs, uint32_t n, uint64_t len) {
+  std::lock_guard<std::mutex> lk(g_ranges_mu);
+  for (uint32_t i = 0; i < n; ++i) {
+    if (!addrs[i]) continue;  // a skipped blob
+    auto it = g_ranges.upper_bound(addrs[i]);
+    if (it == g_ranges.begin()) return false;
+    --it;
+    if (addrs[i] + len > it->first + it->second) return false;
+  }
+  return true;
+}
+
 uint64_t now_ns() {
   return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
              std::chrono::steady_clock::now().time_since_epoch())
@@ -976,6 +1004,7 @@ int kvs_server_create(const kvs_server_config *cfg_in, kvs_server **out) {
   cudaError_t e;
   if ((e = cudaMalloc(&s->slab, cfg.heap_bytes)) != cudaSuccess)
     return fail(set_err(KVS_E_NOSPACE, "slab of %llu B: %s", (unsigned long long)cfg.heap_bytes, cudaGetErrorString(e)));
+  dev_range_add(s->slab, cfg.heap_bytes);
   const uint32_t nb = s->dir->num_buckets();
   if ((e = cudaMalloc(&s->d_buckets, 8ull * nb)) != cudaSuccess ||
       (e = cudaMalloc(&s->d_meta, sizeof(kvs::DevMeta) * cfg.max_keys)) != cudaSuccess ||
@@ -1032,7 +1061,10 @@ int kvs_server_destroy(kvs_server *s) {
     if (s->d_keyrows) cudaFree(s->d_keyrows);
     if (s->d_meta) cudaFree(s->d_meta);
     if (s->d_buckets) cudaFree(s->d_buckets);
-    if (s->slab) cudaFree(s->slab);
+    if (s->slab) {
+      dev_range_remove(s->slab);
+      cudaFree(s->slab);
+    }
     delete s->dir;
   }
   delete s;
@@ -2047,7 +2079,9 @@ int copy_values_launch(kvs_client *c, uint64_t rows, uint64_t value_len, uint32_
   p.tiles_per_combo = meta[4];
   p.total_tiles = (uint64_t)n * p.tiles_per_combo;
   p.to_blob = to_rows ? 0 : 1;
-  CUDA_TRY(launch_copy(p, c->stream, false, c->timeout_flag));
+  // rows are this GPU's memory (checked by the caller): the bulk engine when every value address
+  // lies in a known slab or peer mapping
+  CUDA_TRY(launch_copy(p, c->stream, dev_ranges_hold(addrs, n, value_len), c->timeout_flag));
   return KVS_OK;
 }
 
@@ -2090,6 +2124,11 @@ int kvs_ipc_open(int32_t device, const kvs_ipc_handle *handle, void **base) {
     cudaGetLastError();
     return set_err(KVS_E_CUDA, "ipc_open: %s", cudaGetErrorString(e));
   }
+  GetAddressRangeFn range = address_range_fn();
+  CUdeviceptr b = 0;
+  size_t size = 0;
+  if (range && range(&b, &size, reinterpret_cast<CUdeviceptr>(*base)) == CUDA_SUCCESS)
+    dev_range_add(reinterpret_cast<void *>(b), size);
   return KVS_OK;
 }
 
@@ -2101,6 +2140,7 @@ int kvs_ipc_close(int32_t device, void *base) {
     std::lock_guard<std::mutex> lk(g_checked_mu);
     g_checked_members.clear();
   }
+  dev_range_remove(base);
   CUDA_TRY(cudaIpcCloseMemHandle(base));
   return KVS_OK;
 }
@@ -2302,7 +2342,9 @@ int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, c
   for (uint32_t m = 0; m < layout->n_members; ++m) payload += layout->member_block_bytes[m];
   cudaEvent_t t0 = nullptr;
   c->time_begin(&t0);
-  CUDA_TRY(launch_copy(p, c->stream, false, c->timeout_flag));
+  // members are this GPU's memory (validated): the bulk engine when every value address lies in a
+  // known slab or peer mapping, plain loads and stores otherwise
+  CUDA_TRY(launch_copy(p, c->stream, dev_ranges_hold(blob_addrs, n, fmt.value_len), c->timeout_flag));
   c->time_end(t0, to_blob ? 0 : 1, (uint64_t)n * payload);
   TRY(end_op(c, stream));
   return KVS_OK;
