@@ -329,3 +329,29 @@ def test_profiles_and_counters(store):
     assert not c.is_established()
     with pytest.raises(KvsError, match="closed"):
         c.exists(b"p")
+
+
+def test_put_blocks_with_a_key_twice_in_one_batch_matches_oracle(store):
+    """A batch that puts one key twice: the second put waits for the first to commit (forced
+    commit), then replaces it; the stored value is the second block, state as the oracle's."""
+    n_layers, heads, bs, dim, pool = 2, 2, 16, 64, 32
+    kv = kv_pool(n_layers, heads, bs, dim, pool, seed=3)
+    layout = PagedLayout.from_kv_caches(kv)
+    c, s = store(max_keys=64, heap_bytes=64 * U, host_pool_bytes=8 << 20)
+    o = O.Store(max_keys=64, heap_bytes=64 * U, host_pool_bytes=8 << 20)
+    members = [t for p in kv for t in p]
+    host = [t.view(torch.uint8).reshape(-1).cpu().numpy() for t in members]
+    mb = layout.member_block_bytes
+    keys = np.array([7, 8, 7, 9, 8], dtype=np.uint64)
+    src = np.array([0, 1, 2, 3, 4])
+    c.put_blocks(layout, keys, src)
+    o.put_blocks(host, mb, keys, src)
+    dst = np.array([20, 21, 22])
+    fo = o.get_blocks(host, mb, np.array([7, 8, 9], np.uint64), dst)
+    fs = c.get_blocks(layout, np.array([7, 8, 9], np.uint64), dst)
+    assert fo.all() and fs.all()
+    for m in range(len(members)):
+        got = members[m].view(torch.uint8).reshape(pool, -1)[20:23].cpu().numpy()
+        assert np.array_equal(got, host[m].reshape(pool, -1)[20:23])
+        assert np.array_equal(got[0], host[m].reshape(pool, -1)[2]) and np.array_equal(got[1], host[m].reshape(pool, -1)[4])
+    _compare_state(o, s, [7, 8, 9])

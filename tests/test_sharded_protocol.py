@@ -97,3 +97,43 @@ def test_shard_of_u64_matches_the_c_abi_function():
     keys = np.random.default_rng(2).integers(0, 2**64 - 1, 300, dtype=np.uint64)
     for n in (1, 2, 3, 8):
         assert sharded.shard_of_u64(keys, n).tolist() == [kdist.shard_of(int(k), n) for k in keys]
+
+
+def _empty_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=8)
+        eng = HostEngine(pools[rank], MB, CFG)
+        store = sharded.ShardedStore(eng, max_batch=8, transport="nccl")
+        keys = np.arange(100 + 10 * rank, 104 + 10 * rank, dtype=np.uint64)
+        # rank 1 sits out the put step and rank 0 the get step: every rank still takes every collective
+        store.step((), (), keys if rank == 0 else (), np.arange(4) if rank == 0 else ())
+        got = store.step(np.arange(100, 104, dtype=np.uint64) if rank == 1 else (), np.arange(8, 12) if rank == 1 else ())
+        ex = store.exists_batch(np.arange(98, 106, dtype=np.uint64) if rank == 1 else ())
+        none = store.step()  # nobody has anything
+        q.put((rank, got.tolist(), ex.tolist(), none.tolist(), [m.copy() for m in eng.members]))
+        store.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_protocol_with_empty_batches():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_empty_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = sorted((q.get(timeout=240) for _ in range(world)), key=lambda o: o[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=8)
+    (r0, got0, ex0, none0, _), (r1, got1, ex1, none1, mem1) = out
+    assert got0 == [] and ex0 == [] and none0 == [] and none1 == []
+    assert got1 == [True] * 4 and ex1 == [False, False, True, True, True, True, False, False]
+    for m in range(N_MEMBERS):  # rank 1's blocks 8..11 now hold rank 0's blocks 0..3
+        want = pools[1][m].reshape(N_POOL, MB).copy()
+        want[8:12] = pools[0][m].reshape(N_POOL, MB)[0:4]
+        assert np.array_equal(mem1[m].reshape(N_POOL, MB), want)

@@ -399,6 +399,7 @@ struct kvs_server {
     while (!dir->fifo_empty()) TRY(commit_one());
     retire_batches();
     release_dropped();
+    grant_blocked = false;  // the commit a stopped grant asked for has happened
     return KVS_OK;
   }
 };
@@ -2228,10 +2229,12 @@ int kvs_grant_puts(kvs_client *c, uint32_t n, const uint64_t *keys, uint64_t val
   std::lock_guard<std::mutex> sl(s->mu);
   if (s->grant_blocked) {
     // the prepare that stopped the last grant asked for this commit; its value has landed since
-    TRY(quarantine_on_error(c, s->commit_one()));
-    s->retire_batches();
-    s->release_dropped();
     s->grant_blocked = false;
+    if (!s->dir->fifo_empty() && s->dir->fifo_head().wt_batch >= 0) {
+      TRY(quarantine_on_error(c, s->commit_one()));
+      s->retire_batches();
+      s->release_dropped();
+    }
   }
   uint32_t i = 0;
   for (; i < n; ++i) {
