@@ -55,7 +55,11 @@ def _device_index(device: Any) -> int:
 
 
 def _stream_handle(device: int) -> int:
+    """The caller's current CUDA stream on `device` as a raw handle."""
     torch = _torch()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(device)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -237,6 +241,7 @@ class PagedLayout:
         self._ptrs = (C.c_uint64 * len(members))(*[t.data_ptr() for t in members])
         self._bytes = (C.c_uint64 * len(members))(*bb)
         self.c = _native.BlockLayout(len(members), members_per_layer, self._ptrs, self._bytes, self.num_blocks)
+        self.ref = C.byref(self.c)  # reused by every call
 
     @classmethod
     def from_kv_caches(cls, kv_caches: Iterable[Sequence[Any]]) -> "PagedLayout":
@@ -265,7 +270,15 @@ class PagedLayout:
         return off
 
 
+def _i64_array(values: Any) -> np.ndarray:
+    if isinstance(values, np.ndarray) and values.dtype == np.int64 and values.flags.c_contiguous:
+        return values
+    return np.ascontiguousarray(np.asarray(values, dtype=np.int64))
+
+
 def _u64_keys(keys: Any) -> np.ndarray:
+    if isinstance(keys, np.ndarray) and keys.dtype == np.uint64 and keys.flags.c_contiguous:
+        return keys
     arr = np.asarray(keys)
     if arr.dtype.kind in "iu":
         return np.ascontiguousarray(arr.astype(np.uint64))
@@ -428,38 +441,29 @@ class Client:
         if layout.device != self.device:
             raise RuntimeError(f"put_blocks: layout lives on device {layout.device}, client on {self.device}")
         k = _u64_keys(keys)
-        b = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int64))
+        b = _i64_array(block_ids)
         if k.shape != b.shape:
             raise RuntimeError("put_blocks: keys and block_ids must have equal length")
-        check(
-            load().kvs_put_blocks(
-                self._handle(), C.byref(layout.c), k.size, k.ctypes.data_as(_native._u64p),
-                b.ctypes.data_as(_native._i64p), 1 if sync_commit else 0, _stream_handle(self.device),
-            )
-        )
+        check(load().kvs_put_blocks(self._handle(), layout.ref, k.size, k.ctypes.data, b.ctypes.data,
+                                    1 if sync_commit else 0, _stream_handle(self.device)))
 
     def get_blocks(self, layout: PagedLayout, keys: Any, block_ids: Any) -> np.ndarray:
         if layout.device != self.device:
             raise RuntimeError(f"get_blocks: layout lives on device {layout.device}, client on {self.device}")
         k = _u64_keys(keys)
-        b = np.ascontiguousarray(np.asarray(block_ids, dtype=np.int64))
+        b = _i64_array(block_ids)
         if k.shape != b.shape:
             raise RuntimeError("get_blocks: keys and block_ids must have equal length")
-        found = np.zeros(k.size, np.uint8)
-        check(
-            load().kvs_get_blocks(
-                self._handle(), C.byref(layout.c), k.size, k.ctypes.data_as(_native._u64p),
-                b.ctypes.data_as(_native._i64p), found.ctypes.data_as(_native._u8p), _stream_handle(self.device),
-            )
-        )
-        return found.astype(bool)
+        found = np.zeros(k.size, np.bool_)  # bool is one byte: the C ABI fills it in place
+        check(load().kvs_get_blocks(self._handle(), layout.ref, k.size, k.ctypes.data, b.ctypes.data,
+                                    found.ctypes.data, _stream_handle(self.device)))
+        return found
 
     def exists_batch(self, keys: Any) -> np.ndarray:
         k = _u64_keys(keys)
-        found = np.zeros(k.size, np.uint8)
-        check(load().kvs_exists_batch(self._handle(), k.size, k.ctypes.data_as(_native._u64p),
-                                      found.ctypes.data_as(_native._u8p)))
-        return found.astype(bool)
+        found = np.zeros(k.size, np.bool_)
+        check(load().kvs_exists_batch(self._handle(), k.size, k.ctypes.data, found.ctypes.data))
+        return found
 
     def set_kernel_timing(self, enable: bool) -> None:
         """Bracket every gather / scatter launch with CUDA events on the client stream."""

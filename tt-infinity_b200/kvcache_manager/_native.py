@@ -187,9 +187,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvs_move_to_device": (C.c_int, [P, P, C.c_uint32]),
     "kvs_flush": (C.c_int, [P]),
     "kvs_client_put_profile": (C.c_int, [P, C.POINTER(PutProfile)]),
-    "kvs_put_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, _u64p, _i64p, C.c_int, P]),
-    "kvs_get_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, _u64p, _i64p, _u8p, P]),
-    "kvs_exists_batch": (C.c_int, [P, C.c_uint32, _u64p, _u8p]),
+    # the block calls take array addresses as plain integers (numpy .ctypes.data): the per-call
+    # pointer casts were a measurable part of a one-block get
+    "kvs_put_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, P, P, C.c_int, P]),
+    "kvs_get_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, P, P, P, P]),
+    "kvs_exists_batch": (C.c_int, [P, C.c_uint32, P, P]),
     "kvs_ipc_export": (C.c_int, [P, C.POINTER(IpcHandle), _u64p]),
     "kvs_ipc_open": (C.c_int, [C.c_int32, C.POINTER(IpcHandle), C.POINTER(P)]),
     "kvs_ipc_close": (C.c_int, [C.c_int32, P]),
