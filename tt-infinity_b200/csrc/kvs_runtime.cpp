@@ -891,12 +891,10 @@ int quarantine_on_error(kvs_client *c, int rc) {
   return rc;
 }
 
-// Copy one value between a slab location and a buffer with a copy engine. dst != 0 marks both
-// sides as device memory (bulk engine); 0 means the source is host memory (LDG engine).
-int launch_value_copy(kvs_client *c, uint64_t dst, uint64_t src, uint64_t len, size_t rec_off) {
-  // rec layout: {member ptr(dst buffer), bytes, region base 0, tile prefix[2], blob ptr(src)}
-  uint64_t *r = c->stage.h<uint64_t>(rec_off);
-  (void)r;
+// Copy one value staged by stage_value_copy (record at rec_off) with one copy launch. With
+// device_memory_only both sides are device memory (bulk engine); otherwise the source is the
+// pinned host tier read through its device alias (LDG engine).
+int launch_value_copy(kvs_client *c, size_t rec_off, uint64_t len, bool device_memory_only) {
   kvs::ChunkCopyParams p{};
   p.member_ptrs = c->stage.d<uint64_t>(rec_off);
   p.member_bytes = c->stage.d<uint64_t>(rec_off + 8);
@@ -912,12 +910,12 @@ int launch_value_copy(kvs_client *c, uint64_t dst, uint64_t src, uint64_t len, s
   p.tiles_per_combo = (len + kTileBytes - 1) / kTileBytes;
   p.total_tiles = p.tiles_per_combo;
   p.to_blob = 0;
-  (void)dst;
-  (void)src;
-  CUDA_TRY(launch_copy(p, c->stream, dst != 0, c->timeout_flag));
+  CUDA_TRY(launch_copy(p, c->stream, device_memory_only, c->timeout_flag));
   return KVS_OK;
 }
 
+// Record of a one-value copy src -> dst as a one-member scatter: {member ptr = dst, member bytes,
+// region base 0, tile prefix {0, tiles}, blob ptr = src, block id 0}.
 size_t stage_value_copy(Staging &st, uint64_t dst, uint64_t src, uint64_t len) {
   const size_t off = st.take(56);
   uint64_t *r = st.h<uint64_t>(off);
@@ -1408,7 +1406,7 @@ int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_
   TRY(quarantine_on_error(c, launch_mutations(c, s, pm)));
   if (action == Directory::GetAction::kAdmit)
     CUDA_TRY(cudaMemcpyAsync(s->slab + admit_off, s->host_ptr(hb), len, cudaMemcpyHostToDevice, c->stream));
-  TRY(quarantine_on_error(c, launch_value_copy(c, action == Directory::GetAction::kHostOnly ? 0 : 1, 0, len, rec)));
+  TRY(quarantine_on_error(c, launch_value_copy(c, rec, len, action != Directory::GetAction::kHostOnly)));
   s->launches++;
   TRY(chain_record(c, si));
   CUDA_TRY(cudaStreamSynchronize(c->stream));
