@@ -710,11 +710,19 @@ def run_mix(args, rank, local_rank, world):
         moved = _sum_over_ranks(torch, dist, (c1["gets_found"] - c0["gets_found"] + c1["puts"] - c0["puts"]) * MIX_PAYLOAD,
                                 device)
         dom, kernels, nvl = _nvlink_roofline(torch, dist, device, timing, c0, c1, MIX_PAYLOAD)
-        results[transport] = {"value": round(moved / (ms / 1e3) / GB, 3), "ms_per_step": round(ms / args.steps, 3),
-                              "kernels": kernels, "roofline_kernel": dom,
-                              "nvlink_achieved_GBps": round(nvl, 1),
-                              "nvlink_frac": round(nvl / NVLINK_PEER_GBS, 4), "clocks": clocks,
-                              "grant_rounds_per_step": (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps}
+        entry = {"value": round(moved / (ms / 1e3) / GB, 3), "ms_per_step": round(ms / args.steps, 3),
+                 "kernels": kernels, "clocks": clocks,
+                 "grant_rounds_per_step": (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps}
+        if transport == "p2p":
+            entry.update(roofline_kernel=dom, nvlink_achieved_GBps=round(nvl, 1),
+                         nvlink_frac=round(nvl / NVLINK_PEER_GBS, 4))
+        else:
+            # the copy kernels pack and unpack rows in this GPU's memory; NCCL moves them over NVLink
+            for k in entry["kernels"].values():
+                k.pop("nvlink_bytes_per_launch", None)
+                k.pop("achieved_nvlink_GBps", None)
+            entry["note"] = "kernels copy rows within this GPU; the bytes cross NVLink inside NCCL send/recv"
+        results[transport] = entry
     stats = store.stats()
     store.close()
     hw_mine, hw_min, hw_sum = _host_write_rates(torch, dist, device)
