@@ -798,7 +798,7 @@ def cpu_baseline(seconds: float) -> dict:
     threads = cpu_threads()
     n = 16
     gbps, dt = cpu_run(n, 1, threads)
-    steps = max(1, min(20, int(seconds / max(dt, 1e-3))))
+    steps = max(1, min(2000, int(seconds / max(dt, 1e-3))))  # about `seconds` of CPU work
     gbps, dt = cpu_run(n, steps, threads)
     return {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{steps} steps x (put {n} + get {n}) Qwen3-32B-shaped 16 MiB blocks on a 96-block host pool, "

@@ -190,3 +190,61 @@ def test_sharded_store_two_gpus(transport):
         p.join(timeout=120)
         assert p.exitcode == 0
     _check_against_replay(outs, world, steps, batch)
+
+
+def test_owner_and_copy_entry_points_reject_bad_arguments():
+    """Host-side checks of the process-per-GPU entry points (nothing reaches a kernel)."""
+    import ctypes as C
+
+    from kvcache_manager import Client, KvsError, Server
+
+    lib = load()
+    members = [torch.zeros((8, 512), dtype=torch.uint8, device="cuda") for _ in range(2)]
+    layout = PagedLayout(members, members_per_layer=2)
+    other = PagedLayout([torch.zeros((8, 256), dtype=torch.uint8, device="cuda") for _ in range(2)], members_per_layer=2)
+    s0, s1 = Server(0, max_keys=16, heap_bytes=16 * 4288), Server(0, max_keys=16, heap_bytes=16 * 4288)
+    two = Client(0, [s0, s1])
+    one = Client(0, s0)
+    try:
+        keys = np.arange(1, 3, dtype=np.uint64)
+        offs = np.zeros(2, np.uint64)
+        ng = C.c_uint32()
+        # an owner client has exactly one shard
+        rc = lib.kvs_grant_puts(two._handle(), 2, keys.ctypes.data_as(_native._u64p), 1056,
+                                offs.ctypes.data_as(_native._u64p), C.byref(ng))
+        assert rc == _native.E_INVAL and b"exactly one shard" in lib.kvs_last_error()
+        # a value longer than max_value_bytes
+        rc = lib.kvs_grant_puts(one._handle(), 2, keys.ctypes.data_as(_native._u64p), 1 << 40,
+                                offs.ctypes.data_as(_native._u64p), C.byref(ng))
+        assert rc == _native.E_INVAL
+        # serve_gets: every pool must have the same member sizes; pool index and block range checked
+        pools = (_native.BlockLayout * 2)(layout.c, other.c)
+        sets = np.zeros(1, np.uint32)
+        ids = np.zeros(1, np.int64)
+        found = np.zeros(1, np.uint8)
+        k1 = keys[:1].copy()
+        args = lambda n_sets, ls, st, bi: (one._handle(), n_sets, ls, 1, st.ctypes.data_as(_native._u32p),
+                                           bi.ctypes.data_as(_native._i64p), k1.ctypes.data_as(_native._u64p),
+                                           found.ctypes.data_as(_native._u8p), None)
+        assert lib.kvs_serve_gets(*args(2, pools, sets, ids)) == _native.E_INVAL
+        assert b"other member sizes" in lib.kvs_last_error()
+        assert lib.kvs_serve_gets(*args(1, pools, np.array([3], np.uint32), ids)) == _native.E_INVAL
+        assert lib.kvs_serve_gets(*args(1, pools, sets, np.array([99], np.int64))) == _native.E_INVAL
+        # copy_blocks: 16-byte aligned addresses, block ids inside the pool
+        addr = np.array([members[0].data_ptr() + 8], np.uint64)
+        rc = lib.kvs_copy_blocks(one._handle(), C.byref(layout.c), 1, ids.ctypes.data_as(_native._i64p),
+                                 addr.ctypes.data_as(_native._u64p), 1, None)
+        assert rc == _native.E_INVAL and b"16-byte aligned" in lib.kvs_last_error()
+        addr[0] -= 8
+        rc = lib.kvs_copy_blocks(one._handle(), C.byref(layout.c), 1, np.array([8], np.int64).ctypes.data_as(_native._i64p),
+                                 addr.ctypes.data_as(_native._u64p), 1, None)
+        assert rc == _native.E_INVAL and b"outside" in lib.kvs_last_error()
+        # puts_landed with nothing granted is a no-op
+        assert lib.kvs_puts_landed(one._handle(), None) == _native.OK
+        with pytest.raises(KvsError):
+            check(lib.kvs_grant_puts(two._handle(), 0, None, 1056, None, C.byref(ng)))
+    finally:
+        one.close()
+        two.close()
+        s0.close()
+        s1.close()
