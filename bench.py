@@ -800,9 +800,15 @@ def cpu_baseline(seconds: float) -> dict:
     gbps, dt = cpu_run(n, 1, threads)
     steps = max(1, min(2000, int(seconds / max(dt, 1e-3))))  # about `seconds` of CPU work
     gbps, dt = cpu_run(n, steps, threads)
-    return {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{steps} steps x (put {n} + get {n}) Qwen3-32B-shaped 16 MiB blocks on a 96-block host pool, "
-                      f"{threads} threads, {dt:.1f} s"}
+    out = {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": f"{steps} steps x (put {n} + get {n}) Qwen3-32B-shaped 16 MiB blocks on a 96-block host pool, "
+                     f"{threads} threads, {dt:.1f} s"}
+    if threads > 1:  # the same sample on one core, about a quarter of the time
+        g1, d1 = cpu_run(n, 1, 1)
+        s1 = max(1, min(2000, int(seconds / 4 / max(d1, 1e-3))))
+        g1, d1 = cpu_run(n, s1, 1)
+        out["single_thread"] = {"value": round(g1, 3), "cores": 1, "sample": f"{s1} steps, 1 thread, {d1:.1f} s"}
+    return out
 
 
 def run_reference(args, rank, world):

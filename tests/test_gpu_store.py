@@ -162,6 +162,21 @@ def test_get_blocks_miss_leaves_blocks_untouched(store):
     assert all(torch.equal(a, b) for a, b in zip(before, [t for p in kv for t in p]))
 
 
+@pytest.mark.parametrize("n_keys", [1, 6])
+def test_get_blocks_of_a_value_of_another_length_is_a_format_error(store, n_keys):
+    """A key whose stored value is not one block of the layout: get_blocks reports it and writes
+    nothing for it (n_keys = 1 takes the one-launch probe+scatter path)."""
+    c, s = store()
+    kv = kv_pool(2, 2, 16, 64, 32, seed=4)
+    layout = PagedLayout.from_kv_caches(kv)
+    c.put(5, dev_bytes(payload(5, 1000)), 1000, sync_commit=True)
+    before = [t.clone() for p in kv for t in p]
+    keys = [5] + list(range(100, 100 + n_keys - 1))
+    with pytest.raises(KvsError, match="block layout needs"):
+        c.get_blocks(layout, keys, list(range(n_keys)))
+    assert all(torch.equal(a, b) for a, b in zip(before, [t for p in kv for t in p]))
+
+
 def test_fp8_with_per_block_scales_roundtrip(store):
     """Config-5 style layout: per layer K, V fp8 e4m3 (16-token blocks) plus one fp32 scale per block."""
     c, s = store(max_keys=512, heap_bytes=2048 * U)
@@ -260,12 +275,14 @@ def test_directory_policy_matches_oracle_under_pressure(store, seed):
     assert np.array_equal(dev_b[:, 1], host_b[:, 1]) and np.array_equal(dev_b[live, 0], host_b[live, 0])
 
 
+@pytest.mark.parametrize("get_n", [12, 3])
 @pytest.mark.parametrize("repeat_keys", [False, True])
-def test_block_path_eviction_and_host_tier_matches_oracle(store, repeat_keys):
+def test_block_path_eviction_and_host_tier_matches_oracle(store, repeat_keys, get_n):
     """Blocks under a slab that holds a quarter of them: LRU eviction, host-tier serves and
     read-through admissions on get_blocks, compared with the oracle's sequential semantics. With
     repeat_keys a get batch names some keys more than once (a host-tier key admitted by its first
-    get is read from its new block by the later ones)."""
+    get is read from its new block by the later ones). get_n = 3 takes the one-launch
+    probe+scatter path of small gets."""
     n_layers, heads, bs, dim, pool = 2, 2, 16, 64, 96
     kv = kv_pool(n_layers, heads, bs, dim, pool, seed=7)
     layout = PagedLayout.from_kv_caches(kv)
@@ -285,8 +302,8 @@ def test_block_path_eviction_and_host_tier_matches_oracle(store, repeat_keys):
         src = rng.choice(48, 8, replace=False)
         c.put_blocks(layout, keys[idx], src)
         o.put_blocks(host, mb, keys[idx], src)
-        g = rng.choice(48, 12, replace=repeat_keys)
-        dst = 48 + rng.choice(48, 12, replace=False)
+        g = rng.choice(48, get_n, replace=repeat_keys)
+        dst = 48 + rng.choice(48, get_n, replace=False)
         fo = o.get_blocks(host, mb, keys[g], dst)
         fs = c.get_blocks(layout, keys[g], dst)
         assert np.array_equal(fo, fs)
