@@ -275,6 +275,18 @@ int kvs_paged_fill_varlen(const void *k_fill, const void *v_fill, uint32_t n_hea
                           uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
                           uint32_t max_blocks_per_seq, const int32_t *start_positions, void *cache_k, void *cache_v,
                           uint32_t num_blocks, uint32_t block_size, uint32_t *out_of_range, void *stream);
+/* The same fill for n_layers layers that share the requests and page tables (no counterpart in
+ * the reference, which fills one layer per call): layer l reads k_fills[l] / v_fills[l] and
+ * writes cache_ks[l] / cache_vs[l], every layer of the same shapes. Up to 64 layers go in one
+ * launch, so a restore of a whole model pays one kernel ramp instead of one per layer. Each
+ * layer's result equals kvs_paged_fill_varlen on that layer; *out_of_range counts each skipped
+ * token once (not once per layer). */
+int kvs_paged_fill_varlen_layers(uint32_t n_layers, const void *const *k_fills, const void *const *v_fills,
+                                 uint32_t n_heads, uint32_t total_tokens, uint32_t row_bytes,
+                                 const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
+                                 uint32_t max_blocks_per_seq, const int32_t *start_positions, void *const *cache_ks,
+                                 void *const *cache_vs, uint32_t num_blocks, uint32_t block_size,
+                                 uint32_t *out_of_range, void *stream);
 
 /* ---- chunk gather / scatter ops ----
  * gather_tp_shards_to_chip / pack_local_shards (patch 0003 gather.hpp lines 9372-9417) and

@@ -48,6 +48,76 @@ def test_paged_fill_matches_oracle(seed, aligned):
     assert np.array_equal(got_k, exp_k) and np.array_equal(got_v, exp_v)
 
 
+@pytest.mark.parametrize("case", ["many_requests", "one_head_consecutive_blocks", "row_192B", "row_16KiB", "row_17KiB"])
+def test_paged_fill_edge_cases(case):
+    """32 or more requests (the binary-search lookup instead of the in-register one), one KV head
+    over physically consecutive blocks, and rows of 192 B, 16 KiB and 17 KiB."""
+    import zlib
+
+    rng = np.random.default_rng(zlib.crc32(case.encode()))
+    heads, dim, bs, batch = {"many_requests": (2, 64, 32, 37), "one_head_consecutive_blocks": (1, 128, 16, 4),
+                             "row_192B": (2, 96, 16, 5), "row_16KiB": (1, 8192, 16, 2),
+                             "row_17KiB": (1, 8704, 16, 2)}[case]
+    long_requests = case in ("many_requests", "one_head_consecutive_blocks")  # 32-token multiples
+    k, v, cu, pt, sp, ck, cv, _ = random_case(rng, heads, dim, bs, batch, aligned=long_requests, pad_batch=1)
+    if case == "one_head_consecutive_blocks":
+        pt = np.where(pt != 0, np.arange(1, pt.size + 1).reshape(pt.shape) % ck.shape[0], 0).astype(np.int32)
+    exp_k, exp_v = ck.copy(), cv.copy()
+    n_oor = O.paged_fill_varlen(k, v, cu, pt, sp, exp_k, exp_v)
+    oor = torch.zeros(1, dtype=torch.int32, device="cuda")
+    got_k, got_v = run_gpu(k, v, cu, pt, sp, ck, cv, torch.bfloat16, oor)
+    assert np.array_equal(got_k, exp_k) and np.array_equal(got_v, exp_v)
+    assert int(oor.item()) == n_oor
+
+
+@pytest.mark.parametrize("n_layers", [1, 3, 70])
+def test_paged_fill_layers_matches_oracle_per_layer(n_layers):
+    """The all-layers fill (one launch per 64 layers) gives every layer the oracle's single-layer
+    result, and counts each out-of-range token once."""
+    rng = np.random.default_rng(40 + n_layers)
+    k, v, cu, pt, sp, ck, cv, _ = random_case(rng, 2, 64, 16, 4, aligned=True, pad_batch=1)
+    pt = pt.copy()
+    r = int(np.argmax(np.diff(cu[:5]) > 0))  # a request with tokens: its last block is out of range
+    pt[r, (int(sp[r]) + int(cu[r + 1] - cu[r]) - 1) // 16] = ck.shape[0] + 3
+    dev = lambda a: torch.from_numpy(a.view(np.uint8).copy()).cuda().view(torch.bfloat16)
+    i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).cuda()
+    ks, vs, cks, cvs, exp = [], [], [], [], []
+    n_oor = None
+    for layer in range(n_layers):
+        lk, lv = (rng.integers(0, 1 << 16, k.shape, dtype=np.uint16) for _ in range(2))
+        lck, lcv = (rng.integers(0, 1 << 16, ck.shape, dtype=np.uint16) for _ in range(2))
+        ek, ev = lck.copy(), lcv.copy()
+        n = O.paged_fill_varlen(lk, lv, cu, pt, sp, ek, ev)
+        n_oor = n if n_oor is None else n_oor
+        exp.append((ek, ev))
+        ks.append(dev(lk).reshape(1, *k.shape))
+        vs.append(dev(lv).reshape(1, *v.shape))
+        cks.append(dev(lck).reshape(ck.shape))
+        cvs.append(dev(lcv).reshape(cv.shape))
+    oor = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.paged_fill_cache_varlen_layers(ks, vs, i32(cu), i32(pt), i32(sp), cks, cvs, out_of_range=oor)
+    torch.cuda.synchronize()
+    for layer, (ek, ev) in enumerate(exp):
+        got_k = cks[layer].view(torch.uint8).cpu().numpy().view(np.uint16).reshape(ck.shape)
+        got_v = cvs[layer].view(torch.uint8).cpu().numpy().view(np.uint16).reshape(cv.shape)
+        assert np.array_equal(got_k, ek) and np.array_equal(got_v, ev), f"layer {layer}"
+    assert int(oor.item()) == n_oor
+
+
+def test_paged_fill_layers_validation():
+    z = lambda *s, dt=torch.bfloat16: torch.zeros(*s, dtype=dt, device="cuda")
+    i32 = lambda *s: torch.zeros(*s, dtype=torch.int32, device="cuda")
+    k, c = [z(1, 2, 32, 64), z(1, 2, 32, 64)], [z(4, 2, 32, 64), z(4, 2, 32, 64)]
+    ops.paged_fill_cache_varlen_layers(k, k, i32(2), i32(1, 2), i32(1), c, c)
+    with pytest.raises(RuntimeError, match="same layers"):
+        ops.paged_fill_cache_varlen_layers(k, k[:1], i32(2), i32(1, 2), i32(1), c, c)
+    c5 = [c[0], z(5, 2, 32, 64)]
+    with pytest.raises(RuntimeError, match="first layer's shapes"):
+        ops.paged_fill_cache_varlen_layers(k, k, i32(2), i32(1, 2), i32(1), c5, c5)
+    with pytest.raises(RuntimeError, match="must match cache_k dtype"):
+        ops.paged_fill_cache_varlen_layers(k, k, i32(2), i32(1, 2), i32(1), [c[0], z(4, 2, 32, 64, dt=torch.float32)], c)
+
+
 def test_paged_fill_out_of_range_is_skipped_and_counted():
     rng = np.random.default_rng(9)
     k, v, cu, pt, sp, ck, cv, _ = random_case(rng, 2, 64, 32, 3, aligned=True)

@@ -460,7 +460,9 @@ int copy_ctas_per_sm() {
 
 // ---------------------------------------------------------------- token-granular paged fill
 //
-// One CTA per (32-token chunk, group of heads); the grid has about two CTAs per SM. Every warp
+// One CTA per (32-token chunk, group of heads, layer); heads are grouped only as far as needed
+// for about two CTAs per SM. A launch over many layers streams at HBM rate; one layer alone
+// (67 MB for an 8192-token Qwen3 layer) is bound by the kernel's ramp and tail. Every warp
 // resolves the chunk's 32 destinations itself, lane i for token i (last cu_seqlens entry <= token, unsigned so the -1 padding never
 // matches; then page_table[request][pos / block_size]), and hands them around with shuffles, so
 // no block barrier separates the lookups from the copy (issuing the first round of source loads
@@ -548,7 +550,17 @@ __device__ __forceinline__ long long fill_row_small(const PagedFillParams &p, ui
 
 constexpr int kFillUnroll = 4;  // 16-byte words in flight per thread per round
 
-__global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFillParams p) {
+__device__ __forceinline__ PagedFillParams fill_layer(const PagedFillParams &p0, const FillLayers &L) {
+  PagedFillParams p = p0;  // layer blockIdx.z of the launch
+  p.k_fill = L.k_fill[blockIdx.z];
+  p.v_fill = L.v_fill[blockIdx.z];
+  p.cache_k = L.cache_k[blockIdx.z];
+  p.cache_v = L.cache_v[blockIdx.z];
+  return p;
+}
+
+__global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFillParams p0, const FillLayers L) {
+  const PagedFillParams p = fill_layer(p0, L);
   const uint32_t t0 = blockIdx.x * kFillTokens;
   const uint32_t heads_per = (p.n_heads + gridDim.y - 1) / gridDim.y;
   const uint32_t h0 = blockIdx.y * heads_per;
@@ -589,7 +601,7 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
     bool oor = false;
     const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor)
                                    : (lane < nt ? fill_row_of(p, t0 + lane, &oor) : -1);
-    if (oor && threadIdx.x < 32 && blockIdx.y == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
+    if (oor && threadIdx.x < 32 && blockIdx.y == 0 && blockIdx.z == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
     // warp-uniform trip count (every lane joins the shuffles): run while the warp's lane 0 is in range
     for (uint32_t base = threadIdx.x; base - lane < total; base += kFillThreads * kFillUnroll) {
       uint64_t dst[kFillUnroll];
@@ -616,7 +628,7 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
     bool oor = false;
     const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor)
                                    : (lane < nt ? fill_row_of(p, t0 + lane, &oor) : -1);
-    if (oor && threadIdx.x < 32 && blockIdx.y == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
+    if (oor && threadIdx.x < 32 && blockIdx.y == 0 && blockIdx.z == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
     const uint64_t per_side = (uint64_t)nt * rb;
     const uint64_t total = (uint64_t)(h1 - h0) * 2 * per_side;
     for (uint64_t base = threadIdx.x; base - lane < total; base += kFillThreads) {
@@ -689,17 +701,16 @@ cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream)
   return cudaGetLastError();
 }
 
-cudaError_t launch_paged_fill(const PagedFillParams &p, cudaStream_t stream) {
-  if (p.total_tokens == 0 || p.n_heads == 0) return cudaSuccess;
+cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &L, uint32_t n_layers,
+                              cudaStream_t stream) {
+  if (p.total_tokens == 0 || p.n_heads == 0 || n_layers == 0) return cudaSuccess;
+  if (n_layers > kMaxFillLayers) return cudaErrorInvalidValue;
   // split the heads into groups only as far as needed for about two CTAs per SM
-  const uint32_t chunks = (p.total_tokens + kFillTokens - 1) / kFillTokens;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  uint32_t groups = (2u * (uint32_t)sms + chunks - 1) / chunks;
+  const uint64_t sms = (uint64_t)sm_count();
+  const uint64_t chunks = (p.total_tokens + kFillTokens - 1) / kFillTokens;
+  uint64_t groups = (2 * sms + chunks * n_layers - 1) / (chunks * n_layers);
   groups = groups < 1 ? 1 : (groups > p.n_heads ? p.n_heads : groups);
-  const dim3 grid(chunks, groups);
-  paged_fill_kernel<<<grid, kFillThreads, 0, stream>>>(p);
+  paged_fill_kernel<<<dim3((unsigned)chunks, (unsigned)groups, n_layers), kFillThreads, 0, stream>>>(p, L);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }

@@ -104,6 +104,8 @@ struct MutationParams {
 
 // Token-granular paged KV fill (moreh_paged_fill_cache_varlen): packed K/V rows of several
 // requests into their paged cache blocks through page tables. All arrays are device memory.
+// One launch fills up to kMaxFillLayers layers that share the requests and page tables; the
+// layer's tensors come from FillLayers (k_fill etc. below are set per layer inside the kernels).
 struct PagedFillParams {
   const uint8_t *k_fill, *v_fill;    // [n_heads][total_tokens][row_bytes]
   uint8_t *cache_k, *cache_v;        // [num_blocks][n_heads][block_size][row_bytes]
@@ -112,6 +114,13 @@ struct PagedFillParams {
   const int32_t *start_positions;    // [batch]
   uint32_t n_heads, total_tokens, row_bytes, batch, max_blocks, num_blocks, block_size;
   unsigned int *out_of_range;        // optional: tokens skipped for a position or block out of range
+                                     // (counted once per token, in the first layer)
+};
+
+constexpr uint32_t kMaxFillLayers = 64;
+struct FillLayers {  // by value in the kernel parameters (2 KiB)
+  const uint8_t *k_fill[kMaxFillLayers], *v_fill[kMaxFillLayers];
+  uint8_t *cache_k[kMaxFillLayers], *cache_v[kMaxFillLayers];
 };
 
 // Launch helpers (return cudaError_t of the launch). `grid_ctas` = 0 picks the default
@@ -123,7 +132,8 @@ cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream)
 cudaError_t read_tma_timeouts(unsigned int *count);
 cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream);
 cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream);
-cudaError_t launch_paged_fill(const PagedFillParams &p, cudaStream_t stream);
+cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &layers, uint32_t n_layers,
+                              cudaStream_t stream);
 cudaError_t launch_echo(const uint8_t *in, uint8_t *out, uint32_t n, cudaStream_t stream);
 
 // Host-side FNV-1a 32 (the same function the device probe computes).

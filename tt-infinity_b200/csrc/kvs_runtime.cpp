@@ -2499,36 +2499,44 @@ static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_me
   return KVS_OK;
 }
 
-int kvs_paged_fill_varlen(const void *k_fill, const void *v_fill, uint32_t n_heads, uint32_t total_tokens,
-                          uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
-                          uint32_t max_blocks_per_seq, const int32_t *start_positions, void *cache_k, void *cache_v,
-                          uint32_t num_blocks, uint32_t block_size, uint32_t *out_of_range, void *stream) {
-  const char *op = "paged_fill_varlen";
+static int paged_fill_impl(uint32_t n_layers, const void *const *k_fills, const void *const *v_fills, uint32_t n_heads,
+                           uint32_t total_tokens, uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch,
+                           const int32_t *page_table, uint32_t max_blocks_per_seq, const int32_t *start_positions,
+                           void *const *cache_ks, void *const *cache_vs, uint32_t num_blocks, uint32_t block_size,
+                           uint32_t *out_of_range, void *stream, const char *op) {
+  if (n_layers == 0) return KVS_OK;
+  if (!k_fills || !v_fills || !cache_ks || !cache_vs) return set_err(KVS_E_INVAL, "%s: layer arrays are null", op);
   if (batch == 0) return set_err(KVS_E_INVAL, "%s: page_table must have at least one row", op);
   if (block_size == 0 || row_bytes == 0 || n_heads == 0)
     return set_err(KVS_E_INVAL, "%s: block_size, head row bytes and num_kv_heads must be > 0", op);
   if (max_blocks_per_seq > num_blocks)
     return set_err(KVS_E_INVAL, "%s: max_num_blocks_per_seq (%u) must be <= max_num_blocks (%u)", op,
                    max_blocks_per_seq, num_blocks);
-  const void *ptrs[] = {k_fill, v_fill, cu_seqlens, page_table, start_positions, cache_k, cache_v};
-  const char *names[] = {"k_fill_value", "v_fill_value", "cu_seqlens", "page_table", "start_positions", "cache_k",
-                         "cache_v"};
   int device = -1;
-  for (int i = 0; i < 7; ++i) {
+  auto on_device = [&](const void *ptr, const char *name, uint32_t layer) -> int {
     cudaPointerAttributes a{};
-    if (!ptrs[i] || cudaPointerGetAttributes(&a, ptrs[i]) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+    if (!ptr || cudaPointerGetAttributes(&a, ptr) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
       cudaGetLastError();
-      return set_err(KVS_E_INVAL, "%s: %s must be on device!", op, names[i]);
+      if (n_layers > 1) return set_err(KVS_E_INVAL, "%s: %s of layer %u must be on device!", op, name, layer);
+      return set_err(KVS_E_INVAL, "%s: %s must be on device!", op, name);
     }
     if (device < 0) device = a.device;
     if (a.device != device) return set_err(KVS_E_INVAL, "%s: All tensors must be on the same device!", op);
+    return KVS_OK;
+  };
+  for (uint32_t l = 0; l < n_layers; ++l) {
+    TRY(on_device(k_fills[l], "k_fill_value", l));
+    TRY(on_device(v_fills[l], "v_fill_value", l));
+    if (l == 0) {
+      TRY(on_device(cu_seqlens, "cu_seqlens", 0));
+      TRY(on_device(page_table, "page_table", 0));
+      TRY(on_device(start_positions, "start_positions", 0));
+    }
+    TRY(on_device(cache_ks[l], "cache_k", l));
+    TRY(on_device(cache_vs[l], "cache_v", l));
   }
   DeviceGuard g(device);
   kvs::PagedFillParams p{};
-  p.k_fill = static_cast<const uint8_t *>(k_fill);
-  p.v_fill = static_cast<const uint8_t *>(v_fill);
-  p.cache_k = static_cast<uint8_t *>(cache_k);
-  p.cache_v = static_cast<uint8_t *>(cache_v);
   p.cu_seqlens = cu_seqlens;
   p.page_table = page_table;
   p.start_positions = start_positions;
@@ -2539,9 +2547,39 @@ int kvs_paged_fill_varlen(const void *k_fill, const void *v_fill, uint32_t n_hea
   p.max_blocks = max_blocks_per_seq;
   p.num_blocks = num_blocks;
   p.block_size = block_size;
-  p.out_of_range = out_of_range;
-  CUDA_TRY(kvs::launch_paged_fill(p, static_cast<cudaStream_t>(stream)));
+  for (uint32_t l0 = 0; l0 < n_layers; l0 += kvs::kMaxFillLayers) {
+    const uint32_t nl = std::min<uint32_t>(kvs::kMaxFillLayers, n_layers - l0);
+    kvs::FillLayers L{};
+    for (uint32_t l = 0; l < nl; ++l) {
+      L.k_fill[l] = static_cast<const uint8_t *>(k_fills[l0 + l]);
+      L.v_fill[l] = static_cast<const uint8_t *>(v_fills[l0 + l]);
+      L.cache_k[l] = static_cast<uint8_t *>(cache_ks[l0 + l]);
+      L.cache_v[l] = static_cast<uint8_t *>(cache_vs[l0 + l]);
+    }
+    p.out_of_range = l0 == 0 ? out_of_range : nullptr;  // counted once per token
+    CUDA_TRY(kvs::launch_paged_fill(p, L, nl, static_cast<cudaStream_t>(stream)));
+  }
   return KVS_OK;
+}
+
+int kvs_paged_fill_varlen(const void *k_fill, const void *v_fill, uint32_t n_heads, uint32_t total_tokens,
+                          uint32_t row_bytes, const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
+                          uint32_t max_blocks_per_seq, const int32_t *start_positions, void *cache_k, void *cache_v,
+                          uint32_t num_blocks, uint32_t block_size, uint32_t *out_of_range, void *stream) {
+  return paged_fill_impl(1, &k_fill, &v_fill, n_heads, total_tokens, row_bytes, cu_seqlens, batch, page_table,
+                         max_blocks_per_seq, start_positions, &cache_k, &cache_v, num_blocks, block_size, out_of_range,
+                         stream, "paged_fill_varlen");
+}
+
+int kvs_paged_fill_varlen_layers(uint32_t n_layers, const void *const *k_fills, const void *const *v_fills,
+                                 uint32_t n_heads, uint32_t total_tokens, uint32_t row_bytes,
+                                 const int32_t *cu_seqlens, uint32_t batch, const int32_t *page_table,
+                                 uint32_t max_blocks_per_seq, const int32_t *start_positions, void *const *cache_ks,
+                                 void *const *cache_vs, uint32_t num_blocks, uint32_t block_size,
+                                 uint32_t *out_of_range, void *stream) {
+  return paged_fill_impl(n_layers, k_fills, v_fills, n_heads, total_tokens, row_bytes, cu_seqlens, batch, page_table,
+                         max_blocks_per_seq, start_positions, cache_ks, cache_vs, num_blocks, block_size, out_of_range,
+                         stream, "paged_fill_varlen_layers");
 }
 
 int kvs_gather_chunk(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_members,

@@ -206,6 +206,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         C.c_int,
         [P, P, C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint32, P, C.c_uint32, P, P, P, C.c_uint32, C.c_uint32, P, P],
     ),
+    "kvs_paged_fill_varlen_layers": (
+        C.c_int,
+        [C.c_uint32, C.POINTER(P), C.POINTER(P), C.c_uint32, C.c_uint32, C.c_uint32, P, C.c_uint32, P, C.c_uint32, P,
+         C.POINTER(P), C.POINTER(P), C.c_uint32, C.c_uint32, P, P],
+    ),
     "kvs_client_set_timing": (C.c_int, [P, C.c_int]),
     "kvs_client_timing": (C.c_int, [P, C.POINTER(KernelTiming), C.POINTER(KernelTiming)]),
     "kvs_gather_chunk": (

@@ -123,6 +123,23 @@ def paged_fill_cache_varlen(k_fill_value: Any, v_fill_value: Any, cu_seqlens: An
     slots). out_of_range: optional int32 CUDA tensor of one element, incremented for tokens skipped
     because their position or block is out of range. Asynchronous on the current stream; returns
     (cache_k, cache_v) as the reference's device operation does."""
+    _check_fill(k_fill_value, v_fill_value, cu_seqlens, page_table, start_positions, cache_k, cache_v, out_of_range)
+    torch = _torch()
+    dev = k_fill_value.device
+    heads, total, dim = k_fill_value.shape[1], k_fill_value.shape[2], k_fill_value.shape[3]
+    P = C.c_void_p
+    check(load().kvs_paged_fill_varlen(
+        P(k_fill_value.data_ptr()), P(v_fill_value.data_ptr()), heads, total, dim * k_fill_value.element_size(),
+        P(cu_seqlens.data_ptr()), page_table.shape[0], P(page_table.data_ptr()), page_table.shape[1],
+        P(start_positions.data_ptr()), P(cache_k.data_ptr()), P(cache_v.data_ptr()), cache_k.shape[0],
+        cache_k.shape[2], P(out_of_range.data_ptr() if out_of_range is not None else None),
+        P(torch.cuda.current_stream(dev).cuda_stream)))
+    return cache_k, cache_v
+
+
+def _check_fill(k_fill_value, v_fill_value, cu_seqlens, page_table, start_positions, cache_k, cache_v,
+                out_of_range) -> None:
+    """The reference's validation of one fill (patch 0002 lines 441-545)."""
     torch = _torch()
     ts = {"k_fill_value": k_fill_value, "v_fill_value": v_fill_value, "cu_seqlens": cu_seqlens,
           "page_table": page_table, "start_positions": start_positions, "cache_k": cache_k, "cache_v": cache_v}
@@ -167,12 +184,37 @@ def paged_fill_cache_varlen(k_fill_value: Any, v_fill_value: Any, cu_seqlens: An
         raise RuntimeError(f"cu_seqlens must hold batch_size + 1 = {page_table.shape[0] + 1} entries")
     if out_of_range is not None and (out_of_range.dtype != torch.int32 or out_of_range.device != dev):
         raise RuntimeError("out_of_range must be an int32 tensor on the fill's device")
-    heads, total, dim = k_fill_value.shape[1], k_fill_value.shape[2], k_fill_value.shape[3]
+
+
+def paged_fill_cache_varlen_layers(k_fill_values: Sequence[Any], v_fill_values: Sequence[Any], cu_seqlens: Any,
+                                   page_table: Any, start_positions: Any, cache_ks: Sequence[Any],
+                                   cache_vs: Sequence[Any], out_of_range: Any = None):
+    """paged_fill_cache_varlen for several layers that share the requests and page tables, in one
+    launch per 64 layers (no counterpart in the reference, which fills one layer per call). Layer
+    l fills cache_ks[l] / cache_vs[l] from k_fill_values[l] / v_fill_values[l], every layer
+    validated as the single-layer op validates it and of the first layer's shapes. Each layer's
+    result equals the single-layer fill; out_of_range counts each skipped token once."""
+    torch = _torch()
+    n = len(k_fill_values)
+    if not (len(v_fill_values) == len(cache_ks) == len(cache_vs) == n):
+        raise RuntimeError("k_fill_values, v_fill_values, cache_ks and cache_vs must name the same layers")
+    if n == 0:
+        return cache_ks, cache_vs
+    k0, c0 = k_fill_values[0], cache_ks[0]
+    for l in range(n):
+        _check_fill(k_fill_values[l], v_fill_values[l], cu_seqlens, page_table, start_positions, cache_ks[l],
+                    cache_vs[l], out_of_range)
+        if k_fill_values[l].shape != k0.shape or cache_ks[l].shape != c0.shape or cache_ks[l].dtype != c0.dtype:
+            raise RuntimeError(f"layer {l}: every layer must have the first layer's shapes and dtype")
+        if k_fill_values[l].device != k0.device:
+            raise RuntimeError("All tensors must be on the same device!")
+    heads, total, dim = k0.shape[1], k0.shape[2], k0.shape[3]
     P = C.c_void_p
-    check(load().kvs_paged_fill_varlen(
-        P(k_fill_value.data_ptr()), P(v_fill_value.data_ptr()), heads, total, dim * k_fill_value.element_size(),
+    arr = lambda ts: (P * n)(*[t.data_ptr() for t in ts])
+    check(load().kvs_paged_fill_varlen_layers(
+        n, arr(k_fill_values), arr(v_fill_values), heads, total, dim * k0.element_size(),
         P(cu_seqlens.data_ptr()), page_table.shape[0], P(page_table.data_ptr()), page_table.shape[1],
-        P(start_positions.data_ptr()), P(cache_k.data_ptr()), P(cache_v.data_ptr()), cache_k.shape[0],
-        cache_k.shape[2], P(out_of_range.data_ptr() if out_of_range is not None else None),
-        P(torch.cuda.current_stream(dev).cuda_stream)))
-    return cache_k, cache_v
+        P(start_positions.data_ptr()), arr(cache_ks), arr(cache_vs), c0.shape[0], c0.shape[2],
+        P(out_of_range.data_ptr() if out_of_range is not None else None),
+        P(torch.cuda.current_stream(k0.device).cuda_stream)))
+    return cache_ks, cache_vs
