@@ -314,6 +314,43 @@ def test_block_path_eviction_and_host_tier_matches_oracle(store, repeat_keys, ge
     assert s.stats()["victims_evicted"] > 0 and s.stats()["admissions"] > 0
 
 
+def test_small_gets_once_the_index_is_in_sync_match_oracle(store):
+    """Gets of at most 8 blocks whose shard has no index updates pending and whose layout is on the
+    device already launch without any host-to-device copy (keys and block ids in the kernel
+    parameters): device hits, a host-tier hit, a miss and a repeated key against the oracle, with
+    gets that must upload (pending index updates, another layout) in between."""
+    n_layers, heads, bs, dim, pool = 2, 2, 16, 64, 64
+    kv = kv_pool(n_layers, heads, bs, dim, pool, seed=12)
+    layout = PagedLayout.from_kv_caches(kv)
+    units = -(-layout.value_bytes() // U)
+    heap = 32 * (1 << (units - 1).bit_length()) * U
+    c, s = store(max_keys=64, heap_bytes=heap, host_pool_bytes=32 << 20)
+    o = O.Store(max_keys=64, heap_bytes=heap, host_pool_bytes=32 << 20)
+    members = [t for p in kv for t in p]
+    host = [t.view(torch.uint8).reshape(-1).cpu().numpy() for t in members]
+    mb = layout.member_block_bytes
+    keys = np.array(codec.chained_block_hashes(91, 16), dtype=np.uint64)
+    c.put_blocks(layout, keys[:12], np.arange(12))
+    o.put_blocks(host, mb, keys[:12], np.arange(12))
+    c.move_to_host(int(keys[3]))
+    o.move_to_host(int(keys[3]))
+    other = PagedLayout.from_kv_caches(kv_pool(n_layers, heads, bs, dim, 8, seed=13))
+    c.get_blocks(other, keys[:1], [0])  # another layout: uploads, and applies the pending updates
+    steps = [([0], [40]),                      # the layout the next gets reuse
+             ([3, 1, 14, 1], [41, 42, 43, 44]),  # host-tier hit (admitted), device hit, miss, repeat
+             ([2], [45]),                      # pending updates after the admission: uploads
+             ([5, 6], [46, 47]), ([7], [48]), ([8, 9, 10, 11], [49, 50, 51, 52])]
+    o.get_blocks([h.copy() for h in host], mb, keys[:1], [0])  # the same get (its pool is not compared)
+    for idx, dst in steps:
+        fo = o.get_blocks(host, mb, keys[idx], np.array(dst))
+        fs = c.get_blocks(layout, keys[idx], dst)
+        assert np.array_equal(fo, fs), (idx, fo, fs)
+        for m in range(len(members)):
+            got = members[m].view(torch.uint8).reshape(pool, -1)[torch.as_tensor(dst).cuda()].cpu().numpy()
+            assert np.array_equal(got, host[m].reshape(pool, -1)[dst]), (idx, m)
+        _compare_state(o, s, [int(k) for k in keys])
+
+
 def test_put_batch_and_get_parallel(store):
     c, s = store()
     c2 = Client(0, s)

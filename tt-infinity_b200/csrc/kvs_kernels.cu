@@ -58,6 +58,11 @@ __device__ __forceinline__ void cta_copy(uint8_t *dst, const uint8_t *src, uint6
   }
 }
 
+// Block id of (blob, chunk block) index i: from block_ids, or from the parameters themselves.
+__device__ __forceinline__ int64_t block_id(const ChunkCopyParams &p, uint64_t i) {
+  return p.block_ids ? p.block_ids[i] : p.inline_ids[i];
+}
+
 // Index of (blob, rank, member) in member_ptrs: blobs of member set s use the s-th group of
 // n_ranks x n_members pointers (several requesters' paged pools in one launch).
 __device__ __forceinline__ uint64_t member_index(const ChunkCopyParams &p, uint32_t blob, uint32_t rank, uint32_t m) {
@@ -65,7 +70,7 @@ __device__ __forceinline__ uint64_t member_index(const ChunkCopyParams &p, uint3
   return (set * p.n_ranks + rank) * p.n_members + m;
 }
 
-__global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const ChunkCopyParams p) {
+__global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const __grid_constant__ ChunkCopyParams p) {
   // Header words: one thread per (blob, word) -- gather only.
   if (p.to_blob && p.n_header_words) {
     const uint64_t nh = (uint64_t)p.n_blobs * p.n_header_words;
@@ -97,7 +102,7 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const ChunkCop
     const uint64_t sbb = p.member_bytes[m];
     const uint64_t seg_off = tile_in_seg * p.tile_bytes;
     const uint64_t len = (sbb - seg_off) < p.tile_bytes ? (sbb - seg_off) : p.tile_bytes;
-    const int64_t block = p.block_ids[(uint64_t)blob * p.blocks_per_blob + cb];
+    const int64_t block = block_id(p, (uint64_t)blob * p.blocks_per_blob + cb);
     uint8_t *member = reinterpret_cast<uint8_t *>(p.member_ptrs[member_index(p, blob, r, m)]) +
                       (uint64_t)block * sbb + seg_off;
     uint8_t *blob_ptr = reinterpret_cast<uint8_t *>(blob_base) + p.region_bases[m] +
@@ -181,7 +186,7 @@ struct TileCursor {
     cb = (uint32_t)(bc % p->blocks_per_blob);
     blob = (uint32_t)(bc / p->blocks_per_blob);
     blob_base = blob < p->n_blobs ? p->blob_ptrs[blob] : 0;
-    block = blob < p->n_blobs ? p->block_ids[(uint64_t)blob * p->blocks_per_blob + cb] : 0;
+    block = blob < p->n_blobs ? block_id(*p, (uint64_t)blob * p->blocks_per_blob + cb) : 0;
   }
   __device__ void init(const ChunkCopyParams *pp, uint64_t begin, uint64_t stop) {
     p = pp;
@@ -229,7 +234,7 @@ struct TileCursor {
   }
 };
 
-__global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const ChunkCopyParams p) {
+__global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const __grid_constant__ ChunkCopyParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kTmaStages];
   const uint32_t tid = threadIdx.x;
@@ -335,11 +340,12 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const Chunk
 }
 
 // One warp per key. Lane i holds key word i; lane 0 computes the FNV-1a hash.
-__global__ void index_lookup_kernel(const LookupParams p) {
+__global__ void index_lookup_kernel(const __grid_constant__ LookupParams p) {
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint32_t lane = threadIdx.x & 31;
   if (warp >= p.n) return;
-  const uint8_t *key = p.keys + (uint64_t)warp * p.key_stride;
+  const uint8_t *key = p.keys ? p.keys + (uint64_t)warp * p.key_stride
+                              : reinterpret_cast<const uint8_t *>(&p.inline_keys[warp]);
   const uint32_t klen = p.key_lens ? p.key_lens[warp] : p.key_stride;
   // key word of this lane, zero padded past klen (directory rows are zero padded too)
   uint32_t kw = 0;

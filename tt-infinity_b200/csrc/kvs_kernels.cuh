@@ -52,6 +52,10 @@ struct LookupOut {
   uint32_t pad;
 };
 
+// Small calls carry their keys and block ids in the kernel parameters instead of an uploaded
+// array (no host-to-device copy before the launch).
+constexpr uint32_t kInlineKeys = 8;
+
 // Parameters of one chunk_copy launch. All arrays are device-accessible.
 struct ChunkCopyParams {
   const uint64_t *member_ptrs;   // [n_sets * n_ranks * n_members]
@@ -59,7 +63,7 @@ struct ChunkCopyParams {
   const uint64_t *member_bytes;  // [n_members] bytes of one block of the member
   const uint64_t *region_bases;  // [n_members] member region offset inside a blob
   const uint64_t *tile_prefix;   // [n_members + 1] tiles per member, prefix summed
-  const int64_t *block_ids;      // [n_blobs * blocks_per_blob]
+  const int64_t *block_ids;      // [n_blobs * blocks_per_blob]; nullptr: inline_ids
   const uint64_t *blob_ptrs;     // [n_blobs] blob base addresses; 0 skips the blob
   const uint32_t *header_words;  // [n_header_words] (gather only)
   uint32_t n_header_words;
@@ -72,10 +76,11 @@ struct ChunkCopyParams {
   uint64_t total_tiles;
   int to_blob;               // 1: members -> blob (gather), 0: blob -> members (scatter)
   unsigned int *timeout_flag;  // optional host-mapped word set to 1 if a bounded wait expires
+  int64_t inline_ids[kInlineKeys];  // block ids when block_ids is nullptr (n_blobs * blocks_per_blob <= 8)
 };
 
 struct LookupParams {
-  const uint8_t *keys;      // n keys, `key_stride` bytes apart
+  const uint8_t *keys;      // n keys, `key_stride` bytes apart; nullptr: inline_keys (8-byte keys)
   const uint32_t *key_lens; // nullptr: every key is key_stride bytes
   uint32_t key_stride;
   uint32_t n;
@@ -88,6 +93,7 @@ struct LookupParams {
   uint64_t expected_len;    // 0: any length
   LookupOut *out;
   uint64_t *blob_ptrs;      // optional: slab_base + off for device hits, else 0
+  uint64_t inline_keys[kInlineKeys];  // the keys when `keys` is nullptr (n <= 8, key_stride 8)
 };
 
 struct MutationParams {

@@ -415,6 +415,12 @@ struct kvs_client {
   std::vector<cudaEvent_t> chain_evt;  // per shard
   Staging stage;
   Staging stage2;  // a get's second pass, packed while the first pass's results are still in flight
+  // Device copy of the last block layout's arrays a get uploaded (member pointers, member block
+  // bytes, region bases, tile prefix, back to back), and the host bytes it holds: small gets that
+  // name the same layout read it from here instead of uploading it again.
+  uint8_t *layout_dev = nullptr;
+  size_t layout_cap = 0;
+  std::vector<uint8_t> layout_key;
   bool closed = false, quarantined = false;
   kvs_put_profile prof{};
   std::vector<uint64_t> validated_members;
@@ -1267,6 +1273,7 @@ int kvs_client_destroy(kvs_client *c) {
     if (c->timeout_flag) cudaFreeHost(c->timeout_flag);
     c->stage.release();
     c->stage2.release();
+    if (c->layout_dev) cudaFree(c->layout_dev);
     for (auto e : c->chain_evt)
       if (e) cudaEventDestroy(e);
     if (c->entry_evt) cudaEventDestroy(c->entry_evt);
@@ -1415,7 +1422,8 @@ int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_
     s->mprof.to_device_count++;
     s->moves_completed.fetch_add(1, std::memory_order_relaxed);
   }
-  TRY(end_op(c, stream));
+  // no end_op: the client stream is idle after the synchronise, so the caller's stream has
+  // nothing to wait for
   *found = 1;
   return KVS_OK;
 }
@@ -1627,26 +1635,34 @@ static ShardOrder order_by_shard(const std::vector<uint32_t> &si, size_t n_shard
   return o;
 }
 
+// Probe parameters for n 8-byte keys of shard s (d_keys nullptr: the caller fills inline_keys).
+static kvs::LookupParams lookup_params(kvs_server *s, const uint8_t *d_keys, uint32_t n, kvs::LookupOut *d_out,
+                                       uint64_t *d_blob, uint64_t expected_len) {
+  kvs::LookupParams lp{};
+  lp.keys = d_keys;
+  lp.key_lens = nullptr;
+  lp.key_stride = 8;
+  lp.n = n;
+  lp.buckets = s->d_buckets;
+  lp.bucket_mask = s->dir->num_buckets() - 1;
+  lp.meta = s->d_meta;
+  lp.key_rows = s->d_keyrows;
+  lp.max_keys = s->cfg.max_keys;
+  lp.slab_base = s->slab_base();
+  lp.expected_len = expected_len;
+  lp.out = d_out;
+  lp.blob_ptrs = d_blob;
+  return lp;
+}
+
 // Launch the device index probe for every shard run. keys/out/blob arrays are in shard order.
 static int launch_lookups(kvs_client *c, const ShardOrder &o, const uint8_t *d_keys, kvs::LookupOut *d_out,
                           uint64_t *d_blob, uint64_t expected_len) {
   for (size_t r = 0; r + 1 < o.run_begin.size(); ++r) {
     const uint32_t b0 = o.run_begin[r], b1 = o.run_begin[r + 1];
     kvs_server *s = c->shards[o.run_shard[r]];
-    kvs::LookupParams lp{};
-    lp.keys = d_keys + 8ull * b0;
-    lp.key_lens = nullptr;
-    lp.key_stride = 8;
-    lp.n = b1 - b0;
-    lp.buckets = s->d_buckets;
-    lp.bucket_mask = s->dir->num_buckets() - 1;
-    lp.meta = s->d_meta;
-    lp.key_rows = s->d_keyrows;
-    lp.max_keys = s->cfg.max_keys;
-    lp.slab_base = s->slab_base();
-    lp.expected_len = expected_len;
-    lp.out = d_out + b0;
-    lp.blob_ptrs = d_blob ? d_blob + b0 : nullptr;
+    const kvs::LookupParams lp = lookup_params(s, d_keys + 8ull * b0, b1 - b0, d_out + b0,
+                                               d_blob ? d_blob + b0 : nullptr, expected_len);
     CUDA_TRY(kvs::launch_index_lookup(lp, c->stream));
     s->launches++;
   }
@@ -1686,41 +1702,90 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) need += mutation_upper_bound(c->shards[i]);
   TRY(st.begin(need, c->stream));
+  // the layout arrays, back to back as the device copy holds them
+  const size_t lay_mb = ptr_bytes, lay_rb = lay_mb + 8ull * t.n_members, lay_tp = lay_rb + 8ull * t.n_members;
+  const size_t lay_bytes = lay_tp + 8ull * (t.n_members + 1);
+  thread_local std::vector<uint8_t> lay;
+  lay.resize(lay_bytes);
+  std::memcpy(lay.data(), t.member_ptrs, ptr_bytes);
+  std::memcpy(lay.data() + lay_mb, t.member_bytes, 8ull * t.n_members);
+  std::memcpy(lay.data() + lay_rb, fmt.region_bases.data(), 8ull * t.n_members);
+  std::memcpy(lay.data() + lay_tp, fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
+  // A small get on one shard with no index updates to apply and a layout already on the device
+  // needs no host-to-device copy: its keys and block ids travel in the kernel parameters.
+  bool inline_call = n <= kvs::kInlineKeys && !t.sets && ord.run_shard.size() == 1 &&
+                     c->layout_key.size() == lay_bytes && std::memcmp(c->layout_key.data(), lay.data(), lay_bytes) == 0;
+  if (inline_call) {
+    size_t nb, nm, nk;
+    c->shards[ord.run_shard[0]]->dir->dirty_counts(&nb, &nm, &nk);
+    inline_call = nb + nm + nk == 0;
+  }
   std::vector<PackedMutations> pms(ns);
-  for (size_t i = 0; i < ns; ++i)
-    if (inv[i]) pms[i] = pack_mutations(c->shards[i], st);
-  const size_t keys_off = st.take(8ull * n);
-  const size_t ids_off = st.take(8ull * n);
-  for (uint32_t j = 0; j < n; ++j) {
-    st.h<uint64_t>(keys_off)[j] = keys[ord.perm[j]];
-    st.h<int64_t>(ids_off)[j] = block_ids[ord.perm[j]];
+  size_t keys_off = 0, ids_off = 0, sets_off = 0, lay_off = 0;
+  const uint8_t *lay_dev = c->layout_dev;
+  if (!inline_call) {
+    for (size_t i = 0; i < ns; ++i)
+      if (inv[i]) pms[i] = pack_mutations(c->shards[i], st);
+    keys_off = st.take(8ull * n);
+    ids_off = st.take(8ull * n);
+    for (uint32_t j = 0; j < n; ++j) {
+      st.h<uint64_t>(keys_off)[j] = keys[ord.perm[j]];
+      st.h<int64_t>(ids_off)[j] = block_ids[ord.perm[j]];
+    }
+    if (t.sets) {
+      sets_off = st.take(4ull * n);
+      for (uint32_t j = 0; j < n; ++j) st.h<uint32_t>(sets_off)[j] = t.sets[ord.perm[j]];
+    }
+    lay_off = st.push(lay.data(), lay_bytes);
+    lay_dev = st.d<uint8_t>(lay_off);
   }
-  size_t sets_off = 0;
-  if (t.sets) {
-    sets_off = st.take(4ull * n);
-    for (uint32_t j = 0; j < n; ++j) st.h<uint32_t>(sets_off)[j] = t.sets[ord.perm[j]];
-  }
-  const size_t mp_off = st.push(t.member_ptrs, ptr_bytes);
-  const size_t mb_off = st.push(t.member_bytes, 8ull * t.n_members);
-  const size_t rb_off = st.push(fmt.region_bases.data(), 8ull * t.n_members);
-  const size_t tp_off = st.push(fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
   const size_t upload_bytes = st.used;
   const size_t out_off = st.take(sizeof(kvs::LookupOut) * n);
   const size_t blob_off = st.take(8ull * n);
-  TRY(st.upload(c->stream, upload_bytes));
+  if (!inline_call) {
+    TRY(st.upload(c->stream, upload_bytes));
+    if (!t.sets) {  // keep the layout on the device for the next small gets
+      if (lay_bytes > c->layout_cap) {
+        CUDA_TRY(cudaStreamSynchronize(c->stream));  // the old copy may still be read
+        if (c->layout_dev) cudaFree(c->layout_dev);
+        c->layout_dev = nullptr;
+        c->layout_cap = 0;
+        c->layout_key.clear();
+        CUDA_TRY(cudaMalloc(&c->layout_dev, std::max<size_t>(lay_bytes, 16 << 10)));
+        c->layout_cap = std::max<size_t>(lay_bytes, 16 << 10);
+      }
+      CUDA_TRY(cudaMemcpyAsync(c->layout_dev, st.d<uint8_t>(lay_off), lay_bytes, cudaMemcpyDeviceToDevice,
+                               c->stream));
+      c->layout_key.assign(lay.begin(), lay.end());
+    }
+  }
   for (size_t i = 0; i < ns; ++i)
     if (inv[i]) TRY(chain_wait(c, c->shards[i]));
-  for (size_t i = 0; i < ns; ++i)
-    if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms[i])));
-  TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.hd<kvs::LookupOut>(out_off),
-                                            st.d<uint64_t>(blob_off), fmt.value_len)));
+  if (inline_call) {
+    kvs_server *s = c->shards[ord.run_shard[0]];
+    kvs::LookupParams lp = lookup_params(s, nullptr, n, st.hd<kvs::LookupOut>(out_off), st.d<uint64_t>(blob_off),
+                                         fmt.value_len);
+    for (uint32_t j = 0; j < n; ++j) lp.inline_keys[j] = keys[ord.perm[j]];
+    CUDA_TRY(kvs::launch_index_lookup(lp, c->stream));
+    s->launches++;
+  } else {
+    for (size_t i = 0; i < ns; ++i)
+      if (inv[i]) TRY(quarantine_on_error(c, launch_mutations(c, c->shards[i], pms[i])));
+    TRY(quarantine_on_error(c, launch_lookups(c, ord, st.d<uint8_t>(keys_off), st.hd<kvs::LookupOut>(out_off),
+                                              st.d<uint64_t>(blob_off), fmt.value_len)));
+  }
   kvs::ChunkCopyParams p{};
-  p.member_ptrs = st.d<uint64_t>(mp_off);
+  p.member_ptrs = reinterpret_cast<const uint64_t *>(lay_dev);
   p.blob_sets = t.sets ? st.d<uint32_t>(sets_off) : nullptr;
-  p.member_bytes = st.d<uint64_t>(mb_off);
-  p.region_bases = st.d<uint64_t>(rb_off);
-  p.tile_prefix = st.d<uint64_t>(tp_off);
-  p.block_ids = st.d<int64_t>(ids_off);
+  p.member_bytes = reinterpret_cast<const uint64_t *>(lay_dev + lay_mb);
+  p.region_bases = reinterpret_cast<const uint64_t *>(lay_dev + lay_rb);
+  p.tile_prefix = reinterpret_cast<const uint64_t *>(lay_dev + lay_tp);
+  if (inline_call) {
+    p.block_ids = nullptr;
+    for (uint32_t j = 0; j < n; ++j) p.inline_ids[j] = block_ids[ord.perm[j]];
+  } else {
+    p.block_ids = st.d<int64_t>(ids_off);
+  }
   p.blob_ptrs = st.d<uint64_t>(blob_off);
   p.n_blobs = n;
   p.blocks_per_blob = 1;
@@ -1930,7 +1995,7 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
       return set_err(KVS_E_CUDA, "get_blocks: device index replica disagrees with the catalog for key %u", i);
     }
   }
-  TRY(end_op(c, stream));
+  // no end_op: the client stream is idle after the synchronise above
   if (format_error >= 0)
     return set_err(KVS_E_FORMAT, "get_blocks: stored value for key %d has length %u, the block layout needs %llu",
                    format_error, res[format_error].value_len, (unsigned long long)fmt.value_len);
