@@ -566,7 +566,10 @@ int end_op(kvs_client *c, void *caller) {
 }
 
 int chain_wait(kvs_client *c, kvs_server *s) {
-  if (s->tail) CUDA_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
+  if (!s->tail) return KVS_OK;
+  for (cudaEvent_t e : c->chain_evt)
+    if (e == s->tail) return KVS_OK;  // recorded on this client's own stream: already ordered
+  CUDA_TRY(cudaStreamWaitEvent(c->stream, s->tail, 0));
   return KVS_OK;
 }
 
