@@ -896,7 +896,7 @@ std::vector<kvs_server *> involved_servers(kvs_client *c, const std::vector<uint
 }
 
 int quarantine_on_error(kvs_client *c, int rc) {
-  if (rc == KVS_E_CUDA) c->quarantined = true;
+  if (rc == KVS_E_CUDA && c) c->quarantined = true;
   return rc;
 }
 
@@ -1377,8 +1377,8 @@ int kvs_put_batch(kvs_client *c, uint32_t n, const void *const *keys, const uint
   return put_values(c, n, keys, key_lens, values, value_lens, sync_commit, stream, "put_batch");
 }
 
-int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_t capacity, int *found,
-            uint64_t *value_len, void *stream) {
+static int get_impl(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_t capacity, int *found,
+                    uint64_t *value_len, void *stream) {
   TRY(check_client(c));
   if (!found) return set_err(KVS_E_INVAL, "get: found is null");
   *found = 0;
@@ -1429,6 +1429,11 @@ int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_
   // nothing to wait for
   *found = 1;
   return KVS_OK;
+}
+
+int kvs_get(kvs_client *c, const void *key, uint32_t key_len, void *out, uint64_t capacity, int *found,
+            uint64_t *value_len, void *stream) {
+  return quarantine_on_error(c, get_impl(c, key, key_len, out, capacity, found, value_len, stream));
 }
 
 int kvs_get_parallel(kvs_client *const *clients, uint32_t n, const void *const *keys, const uint32_t *key_lens,
@@ -1513,7 +1518,7 @@ int kvs_move_to_host(kvs_client *c, const void *key, uint32_t key_len) {
   return KVS_OK;
 }
 
-int kvs_move_to_device(kvs_client *c, const void *key, uint32_t key_len) {
+static int move_to_device_impl(kvs_client *c, const void *key, uint32_t key_len) {
   if (!c) return set_err(KVS_E_INVAL, "client handle is null");
   std::lock_guard<std::mutex> lk(c->mu);
   DeviceGuard g(c->device);
@@ -1544,6 +1549,10 @@ int kvs_move_to_device(kvs_client *c, const void *key, uint32_t key_len) {
   s->mprof.to_device_complete_ns += now_ns() - t0;
   s->moves_completed.fetch_add(1, std::memory_order_relaxed);
   return KVS_OK;
+}
+
+int kvs_move_to_device(kvs_client *c, const void *key, uint32_t key_len) {
+  return quarantine_on_error(c, move_to_device_impl(c, key, key_len));
 }
 
 int kvs_flush(kvs_client *c) {
@@ -2016,10 +2025,10 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
   DeviceGuard g(c->device);
   TRY(validate_layout_ptrs(c, layout, "get_blocks"));
   GetTarget t{&fmt, layout->n_members, layout->member_block_bytes, 1, layout->member_ptrs, nullptr};
-  return get_blocks_impl(c, t, n, keys, block_ids, found, stream);
+  return quarantine_on_error(c, get_blocks_impl(c, t, n, keys, block_ids, found, stream));
 }
 
-int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found) {
+static int exists_batch_impl(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found) {
   TRY(check_client(c));
   if (n == 0) return KVS_OK;
   if (!keys || !found) return set_err(KVS_E_INVAL, "exists_batch: null argument");
@@ -2066,6 +2075,10 @@ int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *f
     }
   }
   return KVS_OK;
+}
+
+int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found) {
+  return quarantine_on_error(c, exists_batch_impl(c, n, keys, found));
 }
 
 // ---------------------------------------------------------------------------- shards in other processes
@@ -2253,7 +2266,7 @@ int kvs_serve_gets(kvs_client *c, uint32_t n_sets, const kvs_block_layout *layou
   for (uint32_t k = 0; k < n_sets; ++k)
     std::memcpy(ptrs.data() + (size_t)k * nm, layouts[k].member_ptrs, 8ull * nm);
   GetTarget t{&fmt, nm, layouts[0].member_block_bytes, n_sets, ptrs.data(), sets};
-  return get_blocks_impl(c, t, n, keys, block_ids, found, stream);
+  return quarantine_on_error(c, get_blocks_impl(c, t, n, keys, block_ids, found, stream));
 }
 
 int kvs_serve_gets_packed(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *keys,
@@ -2277,7 +2290,7 @@ int kvs_serve_gets_packed(kvs_client *c, void *rows, uint64_t value_len, uint32_
   std::vector<int64_t> ids(n);
   for (uint32_t i = 0; i < n; ++i) ids[i] = i;
   GetTarget t{&fmt, 1, &member_bytes, 1, &member_ptr, nullptr};
-  return get_blocks_impl(c, t, n, keys, ids.data(), found, stream);
+  return quarantine_on_error(c, get_blocks_impl(c, t, n, keys, ids.data(), found, stream));
 }
 
 int kvs_grant_puts(kvs_client *c, uint32_t n, const uint64_t *keys, uint64_t value_len, uint64_t *slab_offsets,
@@ -2333,7 +2346,7 @@ int kvs_grant_puts(kvs_client *c, uint32_t n, const uint64_t *keys, uint64_t val
   return KVS_OK;
 }
 
-int kvs_puts_landed(kvs_client *c, void *stream) {
+static int puts_landed_impl(kvs_client *c, void *stream) {
   kvs_server *s = nullptr;
   TRY(owner_shard(c, "puts_landed", &s));
   std::lock_guard<std::mutex> lk(c->mu);
@@ -2363,8 +2376,12 @@ int kvs_puts_landed(kvs_client *c, void *stream) {
   return KVS_OK;
 }
 
-int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const int64_t *block_ids,
-                    const uint64_t *blob_addrs, int to_blob, void *stream) {
+int kvs_puts_landed(kvs_client *c, void *stream) {
+  return quarantine_on_error(c, puts_landed_impl(c, stream));
+}
+
+static int copy_blocks_impl(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const int64_t *block_ids,
+                            const uint64_t *blob_addrs, int to_blob, void *stream) {
   TRY(check_client(c));
   BlockFormat fmt;
   TRY(block_format(layout, &fmt));
@@ -2417,6 +2434,11 @@ int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, c
   c->time_end(t0, to_blob ? 0 : 1, (uint64_t)n * payload);
   TRY(end_op(c, stream));
   return KVS_OK;
+}
+
+int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const int64_t *block_ids,
+                    const uint64_t *blob_addrs, int to_blob, void *stream) {
+  return quarantine_on_error(c, copy_blocks_impl(c, layout, n, block_ids, blob_addrs, to_blob, stream));
 }
 
 int kvs_copy_values(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *addrs, int to_rows,
