@@ -1725,8 +1725,9 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
   std::memcpy(lay.data() + lay_tp, fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
   // A small get on one shard with no index updates to apply and a layout already on the device
   // needs no host-to-device copy: its keys and block ids travel in the kernel parameters.
-  bool inline_call = n <= kvs::kInlineKeys && !t.sets && ord.run_shard.size() == 1 &&
-                     c->layout_key.size() == lay_bytes && std::memcmp(c->layout_key.data(), lay.data(), lay_bytes) == 0;
+  const bool layout_cached = !t.sets && c->layout_key.size() == lay_bytes &&
+                             std::memcmp(c->layout_key.data(), lay.data(), lay_bytes) == 0;
+  bool inline_call = layout_cached && n <= kvs::kInlineKeys && ord.run_shard.size() == 1;
   if (inline_call) {
     size_t nb, nm, nk;
     c->shards[ord.run_shard[0]]->dir->dirty_counts(&nb, &nm, &nk);
@@ -1756,7 +1757,7 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
   const size_t blob_off = st.take(8ull * n);
   if (!inline_call) {
     TRY(st.upload(c->stream, upload_bytes));
-    if (!t.sets) {  // keep the layout on the device for the next small gets
+    if (!t.sets && !layout_cached) {  // keep the layout on the device for the next small gets
       if (lay_bytes > c->layout_cap) {
         CUDA_TRY(cudaStreamSynchronize(c->stream));  // the old copy may still be read
         if (c->layout_dev) cudaFree(c->layout_dev);
