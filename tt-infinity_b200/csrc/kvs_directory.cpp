@@ -48,6 +48,10 @@ Directory::Directory(const DirConfig &cfg) : cfg_(cfg) {
   buckets_.assign(2ull * nb_, 0);
   for (uint32_t b = 0; b < nb_; ++b) buckets_[2 * b + 1] = kBucketEmpty;
   dir_.resize(cfg.max_keys);
+  access64_.assign(cfg.max_keys, 0);
+  rec_prev_.assign(cfg.max_keys, kNone);
+  rec_next_.assign(cfg.max_keys, kNone);
+  rec_linked_.assign(cfg.max_keys, 0);
   free_next_.assign(cfg.max_keys, kNone);
   lru_prev_.assign(cfg.max_keys, kNone);
   lru_next_.assign(cfg.max_keys, kNone);
@@ -305,6 +309,56 @@ void Directory::drop_backing(uint32_t slot) {
   h = HostBacking{};
 }
 
+uint32_t Directory::bump_epoch() {
+  ++epoch64_;
+  return ++epoch_;
+}
+
+void Directory::rec_unlink(uint32_t slot) {
+  if (!rec_linked_[slot]) return;
+  const uint32_t p = rec_prev_[slot], n = rec_next_[slot];
+  if (p != kNone) rec_next_[p] = n; else rec_head_ = n;
+  if (n != kNone) rec_prev_[n] = p; else rec_tail_ = p;
+  rec_prev_[slot] = rec_next_[slot] = kNone;
+  rec_linked_[slot] = 0;
+}
+
+// The slot's entry was just given the newest access epoch: it moves to the tail.
+void Directory::rec_touch(uint32_t slot) {
+  rec_unlink(slot);
+  rec_prev_[slot] = rec_tail_;
+  rec_next_[slot] = kNone;
+  if (rec_tail_ != kNone) rec_next_[rec_tail_] = slot; else rec_head_ = slot;
+  rec_tail_ = slot;
+  rec_linked_[slot] = 1;
+  access64_[slot] = epoch64_;
+}
+
+// The catalog replacement victim (P3:10373-10413): the valid, non-pending entry with the largest
+// 32-bit access age, epoch - last_access; kNone if every valid entry is pending. Access epochs are
+// unique, so while the oldest entry is younger than 2^32 epochs the 32-bit ages order the entries
+// as the access list does and the first non-pending entry from its head is the answer; past that
+// the reference's wrap-around arithmetic decides, by its own scan over every slot.
+uint32_t Directory::oldest_replaceable() const {
+  if (rec_head_ == kNone) return kNone;
+  if (epoch64_ - access64_[rec_head_] < (1ull << 32)) {
+    for (uint32_t i = rec_head_; i != kNone; i = rec_next_[i])
+      if (dir_[i].location != kLocPending) return i;
+    return kNone;
+  }
+  uint32_t oldest = kNone, oldest_age = 0;
+  for (uint32_t i = 0; i < cfg_.max_keys; ++i) {
+    const Entry &e = dir_[i];
+    if (!e.valid || e.location == kLocPending) continue;
+    const uint32_t age = epoch_ - e.last_access;
+    if (oldest == kNone || age > oldest_age) {
+      oldest_age = age;
+      oldest = i;
+    }
+  }
+  return oldest;
+}
+
 Prepare Directory::prepare_put(const uint8_t *key, uint32_t len, uint64_t value_len, Grant *out) {
   const uint64_t units = units_for(value_len);
   const uint32_t h = hash_of(key, len);
@@ -313,19 +367,8 @@ Prepare Directory::prepare_put(const uint8_t *key, uint32_t len, uint64_t value_
   if (slot != kBucketEmpty) retry = dir_[slot].location == kLocPending;
   if (!retry && slot == kBucketEmpty) slot = catalog_claim();
   if (!retry && slot == kBucketEmpty) {
-    uint32_t oldest = 0, oldest_age = 0;
-    bool have = false;
-    for (uint32_t i = 0; i < cfg_.max_keys; ++i) {
-      const Entry &e = dir_[i];
-      if (!e.valid || e.location == kLocPending) continue;
-      const uint32_t age = epoch_ - e.last_access;
-      if (!have || age > oldest_age) {
-        have = true;
-        oldest_age = age;
-        oldest = i;
-      }
-    }
-    if (have) {
+    const uint32_t oldest = oldest_replaceable();
+    if (oldest != kNone) {
       slot = oldest;
       st_.catalog_replacements++;
     } else {
@@ -343,6 +386,7 @@ Prepare Directory::prepare_put(const uint8_t *key, uint32_t len, uint64_t value_
         live_bytes_ = live_bytes_ >= bb ? live_bytes_ - bb : 0;
       }
       old.valid = 0;
+      rec_unlink(slot);
       mark_slot(slot);
       drop_backing(slot);
     }
@@ -354,7 +398,8 @@ Prepare Directory::prepare_put(const uint8_t *key, uint32_t len, uint64_t value_
       e.valid = 1;
       e.key_len = (uint8_t)len;
       e.total_len = value_len;
-      e.last_access = ++epoch_;
+      e.last_access = bump_epoch();
+      rec_touch(slot);
       e.value_off = (uint64_t)unit * cfg_.unit_bytes;
       e.host_gen = token;
       e.location = kLocPending;
@@ -384,7 +429,7 @@ Prepare Directory::prepare_put(const uint8_t *key, uint32_t len, uint64_t value_
 
 bool Directory::commit_head(HostBacking *released) {
   PendingPut it = fifo_.front();
-  fifo_.erase(fifo_.begin());
+  fifo_.pop_front();
   st_.committed++;
   Entry &e = dir_[it.slot];
   if (!e.valid || e.location != kLocPending || e.host_gen != it.token) {
@@ -407,7 +452,8 @@ bool Directory::commit_head(HostBacking *released) {
 
 Directory::GetAction Directory::get_hit(uint32_t slot, uint64_t *admit_off) {
   Entry &e = dir_[slot];
-  const uint32_t epoch = ++epoch_;
+  const uint32_t epoch = bump_epoch();
+  rec_touch(slot);  // every branch below gives the entry this epoch
   if (e.location != kLocHost) {
     e.last_access = epoch;
     lru_touch(slot);
@@ -442,6 +488,7 @@ void Directory::remove(uint32_t slot) {
     if (e.location == kLocPending) pending_bytes_ -= bb;
   }
   e.valid = 0;
+  rec_unlink(slot);
   mark_slot(slot);
   catalog_release(slot);
   drop_backing(slot);
@@ -460,7 +507,8 @@ bool Directory::move_to_device(uint32_t slot, uint64_t *admit_off) {
   e.value_off = (uint64_t)unit * cfg_.unit_bytes;
   e.location = kLocDevice;
   e.order = order;
-  e.last_access = ++epoch_;
+  e.last_access = bump_epoch();
+  rec_touch(slot);
   mark_slot(slot);
   lru_insert_mru(slot);
   live_bytes_ += block_bytes(order);

@@ -22,6 +22,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <deque>
 #include <map>
 #include <vector>
 
@@ -103,7 +104,7 @@ class Directory {
   size_t fifo_size() const { return fifo_.size(); }
   PendingPut &fifo_head() { return fifo_.front(); }
   PendingPut &fifo_back() { return fifo_.back(); }
-  std::vector<PendingPut> &fifo() { return fifo_; }
+  std::deque<PendingPut> &fifo() { return fifo_; }
   // Commit the head: install its backing (returns false for a stale token, whose reserved
   // backing is handed back through *released for the caller to free).
   bool commit_head(HostBacking *released);
@@ -168,6 +169,10 @@ class Directory {
   void lru_insert_mru(uint32_t slot);
   void lru_touch(uint32_t slot);
   // catalog
+  uint32_t bump_epoch();
+  void rec_unlink(uint32_t slot);
+  void rec_touch(uint32_t slot);
+  uint32_t oldest_replaceable() const;
   uint32_t catalog_claim();
   void catalog_release(uint32_t slot);
   void drop_backing(uint32_t slot);
@@ -189,8 +194,16 @@ class Directory {
   uint32_t free_heads_[32];
   uint64_t live_bytes_ = 0, pending_bytes_ = 0;
   uint32_t epoch_ = 0;
+  // Access order of the valid entries (head = least recently accessed) with a 64-bit copy of
+  // each entry's access epoch: while every entry was accessed within the last 2^32 epochs, the
+  // oldest non-pending entry from the head is the reference's replacement victim.
+  uint64_t epoch64_ = 0;
+  std::vector<uint64_t> access64_;
+  std::vector<uint32_t> rec_prev_, rec_next_;
+  std::vector<uint8_t> rec_linked_;
+  uint32_t rec_head_ = kNone, rec_tail_ = kNone;
   uint32_t next_token_ = 1;
-  std::vector<PendingPut> fifo_;  // front = oldest (vector used as a queue; small)
+  std::deque<PendingPut> fifo_;  // front = oldest
   std::vector<HostBacking> host_;
   std::map<uint64_t, uint64_t> pool_free_;  // unit -> units, address ordered
   std::vector<HostBacking> dropped_;
