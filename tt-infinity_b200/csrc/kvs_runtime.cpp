@@ -224,6 +224,12 @@ struct kvs_server {
   std::vector<cudaEvent_t> free_events;
   uint64_t next_batch = 1;
   std::multimap<uint64_t, uint8_t *> heap_cache;  // recycled pinned buffers for off-pool values
+  // Off-pool values live in pinned chunks of at least kHeapChunk bytes, handed out front to back
+  // (one pinning call per chunk rather than per value); the chunks are freed with the shard.
+  static constexpr uint64_t kHeapChunk = 256ull << 20;
+  std::vector<uint8_t *> heap_chunks;
+  uint8_t *heap_next = nullptr;
+  uint64_t heap_left = 0;
   std::atomic<uint64_t> moves_completed{0};
   std::atomic<uint64_t> launches{0};
   kvs_move_profile mprof{};
@@ -297,9 +303,18 @@ struct kvs_server {
         b.heap = it->second;
         heap_cache.erase(it);
       } else {
-        void *p = nullptr;
-        CUDA_TRY(cudaHostAlloc(&p, len, cudaHostAllocPortable | cudaHostAllocMapped));
-        b.heap = (uint8_t *)p;
+        const uint64_t take = (len + 255) & ~uint64_t(255);
+        if (take > heap_left) {
+          void *p = nullptr;
+          const uint64_t chunk = std::max(kHeapChunk, take);
+          CUDA_TRY(cudaHostAlloc(&p, chunk, cudaHostAllocPortable | cudaHostAllocMapped));
+          heap_chunks.push_back((uint8_t *)p);
+          heap_next = (uint8_t *)p;
+          heap_left = chunk;
+        }
+        b.heap = heap_next;
+        heap_next += take;
+        heap_left -= take;
       }
       b.len = len;
     }
@@ -1053,17 +1068,7 @@ int kvs_server_destroy(kvs_server *s) {
     if (s->wt_stream) cudaStreamSynchronize(s->wt_stream);
     for (auto &b : s->wt_batches) cudaEventDestroy(b.done);
     for (auto e : s->free_events) cudaEventDestroy(e);
-    if (s->dir) {
-      for (uint32_t i = 0; i < s->cfg.max_keys; ++i) {
-        HostBacking &hb = s->dir->backing(i);
-        if (hb.present && !hb.in_pool && hb.heap) cudaFreeHost(hb.heap);
-      }
-      for (auto &p : s->dir->fifo())
-        if (p.backing.present && !p.backing.in_pool && p.backing.heap) cudaFreeHost(p.backing.heap);
-      for (auto &b : s->dir->take_dropped())
-        if (!b.in_pool && b.heap) cudaFreeHost(b.heap);
-    }
-    for (auto &kv : s->heap_cache) cudaFreeHost(kv.second);
+    for (uint8_t *chunk : s->heap_chunks) cudaFreeHost(chunk);  // every off-pool value lives in one
     if (s->wt_stream) cudaStreamDestroy(s->wt_stream);
     if (s->pool) cudaFreeHost(s->pool);
     if (s->d_keyrows) cudaFree(s->d_keyrows);
