@@ -421,6 +421,9 @@ struct kvs_server {
 
 // ============================================================================ client
 
+// Bumped whenever a peer mapping closes: member pointers checked before may now be invalid.
+static std::atomic<uint64_t> g_mapping_generation{1};
+
 struct kvs_client {
   int device = 0;
   std::vector<kvs_server *> shards;
@@ -439,6 +442,7 @@ struct kvs_client {
   bool closed = false, quarantined = false;
   kvs_put_profile prof{};
   std::vector<uint64_t> validated_members;
+  uint64_t validated_generation = 0;  // g_mapping_generation when validated_members was checked
   // kernel timing (events around copy-engine launches)
   unsigned int *timeout_flag = nullptr;  // host-mapped word a copy kernel sets if a bounded wait expires
   bool timing = false;
@@ -716,10 +720,12 @@ int block_format(const kvs_block_layout *L, BlockFormat *f) {
 
 int validate_layout_ptrs(kvs_client *c, const kvs_block_layout *L, const char *op) {
   std::vector<uint64_t> cur(L->member_ptrs, L->member_ptrs + L->n_members);
-  if (cur == c->validated_members) return KVS_OK;
+  const uint64_t gen = g_mapping_generation.load(std::memory_order_acquire);
+  if (cur == c->validated_members && c->validated_generation == gen) return KVS_OK;
   for (uint32_t m = 0; m < L->n_members; ++m)
     TRY(check_device_ptr(c, reinterpret_cast<const void *>(L->member_ptrs[m]), op, "member tensor"));
   c->validated_members = cur;
+  c->validated_generation = gen;
   return KVS_OK;
 }
 
@@ -2226,6 +2232,7 @@ int kvs_ipc_close(int32_t device, void *base) {
     std::lock_guard<std::mutex> lk(g_checked_mu);
     g_checked_members.clear();
   }
+  g_mapping_generation.fetch_add(1, std::memory_order_acq_rel);
   dev_range_remove(base);
   CUDA_TRY(cudaIpcCloseMemHandle(base));
   return KVS_OK;
