@@ -351,6 +351,36 @@ def test_small_gets_once_the_index_is_in_sync_match_oracle(store):
         _compare_state(o, s, [int(k) for k in keys])
 
 
+@pytest.mark.parametrize("slab_blocks", [1400, 300])
+def test_put_of_more_than_512_blocks_matches_oracle(store, slab_blocks):
+    """A put of 1100 blocks launches its gather in pieces of 512 while the host prepares the rest;
+    with a slab of 300 blocks the pieces interleave with evictions and forced commits. The catalog,
+    the restored blocks and the found flags equal the oracle's."""
+    n_layers, heads, bs, dim, pool = 2, 2, 16, 32, 2304
+    kv = kv_pool(n_layers, heads, bs, dim, pool, seed=21)
+    layout = PagedLayout.from_kv_caches(kv)
+    units = -(-layout.value_bytes() // U)
+    heap = slab_blocks * (1 << (units - 1).bit_length()) * U
+    cfg = dict(max_keys=2048, heap_bytes=heap, host_pool_bytes=1200 * units * U)
+    c, s = store(**cfg)
+    o = O.Store(**cfg)
+    members = [t for p in kv for t in p]
+    host = [t.view(torch.uint8).reshape(-1).cpu().numpy() for t in members]
+    mb = layout.member_block_bytes
+    keys = np.array(codec.chained_block_hashes(123, 1100), dtype=np.uint64)
+    src = np.random.default_rng(4).permutation(1100)
+    c.put_blocks(layout, keys, src)
+    o.put_blocks(host, mb, keys, src)
+    dst = np.arange(1152, 1152 + 1100)
+    fo = o.get_blocks(host, mb, keys, dst)
+    fs = c.get_blocks(layout, keys, dst)
+    assert np.array_equal(fo, fs) and fs.all()
+    for m in range(len(members)):
+        got = members[m].view(torch.uint8).reshape(pool, -1)[1152:2252].cpu().numpy()
+        assert np.array_equal(got, host[m].reshape(pool, -1)[1152:2252])
+    _compare_state(o, s, [int(k) for k in keys[::7]])
+
+
 def test_put_batch_and_get_parallel(store):
     c, s = store()
     c2 = Client(0, s)
