@@ -34,6 +34,7 @@ import re
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -107,7 +108,8 @@ class ClockSampler:
     def __init__(self, gpu_indices):
         self.proc = None
         self.gpus = gpu_indices
-        self.path = ROOT / "gpurun_out" / f"clocks_{os.getpid()}.csv"
+        # KVS_CLOCKS_DIR keeps the raw samples; by default they go to the temporary directory
+        self.path = Path(os.environ.get("KVS_CLOCKS_DIR", tempfile.gettempdir())) / f"clocks_{os.getpid()}.csv"
 
     def start(self):
         try:
