@@ -1065,6 +1065,19 @@ def run_fill(args):
             tok += n
 
     check_layer(7)
+    # the same per-layer calls back to back, one event pair around all of them (a restore loop
+    # over layers; consecutive fills may overlap launch and drain)
+    seq_times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(50_000_000)
+        e0.record(stream)
+        for (kf, vf), (ck, cv) in zip(fills, caches):
+            ops.paged_fill_cache_varlen(kf, vf, cu, pt, sp, ck, cv)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        seq_times.append(e0.elapsed_time(e1) / layers)
+    check_layer(layers - 2)
     # every layer in one launch (paged_fill_cache_varlen_layers), same inputs, caches zeroed first
     for ck, cv in caches:
         ck.zero_()
@@ -1090,6 +1103,8 @@ def run_fill(args):
     avg_ms = statistics.mean(times)
     achieved = bytes_per_launch / (avg_ms / 1e3) / GB
     peak, kind = measured_peaks()
+    seq_ms = statistics.mean(seq_times)
+    seq_achieved = bytes_per_launch / (seq_ms / 1e3) / GB
     all_ms = statistics.mean(all_times)
     all_achieved = layers * bytes_per_launch / (all_ms / 1e3) / GB
     return {"fill": "moreh_paged_fill_cache_varlen restated token-granular: 8192 tokens, 4 requests, 8 KV heads x 128 "
@@ -1098,6 +1113,11 @@ def run_fill(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind,
                          "frac": round(achieved / peak, 4), "unit": "GB/s"},
             "restore_64_layers_ms": round(avg_ms * layers, 3),
+            "per_layer_calls_back_to_back": {"layers": layers, "steps": len(seq_times),
+                                             "avg_per_layer_ms": round(seq_ms, 4),
+                                             "roofline": {"bound": "hbm", "achieved": round(seq_achieved, 1),
+                                                          "peak": peak, "frac": round(seq_achieved / peak, 4),
+                                                          "unit": "GB/s"}},
             "all_layers_one_launch": {"launches": len(all_times), "avg_launch_ms": round(all_ms, 4),
                                       "roofline": {"bound": "hbm", "achieved": round(all_achieved, 1), "peak": peak,
                                                    "frac": round(all_achieved / peak, 4), "unit": "GB/s"}}}
