@@ -654,8 +654,14 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
   }
 }
 
+// Block ids from the parameters cover at most kInlineKeys (blob, chunk block) pairs.
+static bool inline_ids_fit(const ChunkCopyParams &p) {
+  return p.block_ids || (uint64_t)p.n_blobs * p.blocks_per_blob <= kInlineKeys;
+}
+
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas) {
   if (p.total_tiles == 0 && (p.n_header_words == 0 || !p.to_blob)) return cudaSuccess;
+  if (!inline_ids_fit(p)) return cudaErrorInvalidValue;
   uint64_t grid = grid_ctas > 0 ? (uint64_t)grid_ctas : (uint64_t)sm_count() * copy_ctas_per_sm();
   if (grid > p.total_tiles && p.total_tiles > 0) grid = p.total_tiles;
   if (grid == 0) grid = 1;
@@ -666,6 +672,7 @@ cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int
 
 cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream) {
   if (p.total_tiles == 0 && (p.n_header_words == 0 || !p.to_blob)) return cudaSuccess;
+  if (!inline_ids_fit(p)) return cudaErrorInvalidValue;
   static thread_local int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -689,6 +696,7 @@ cudaError_t read_tma_timeouts(unsigned int *count) {
 
 cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream) {
   if (p.n == 0) return cudaSuccess;
+  if (!p.keys && (p.n > kInlineKeys || p.key_stride != 8 || p.key_lens)) return cudaErrorInvalidValue;
   const uint32_t threads = 256, warps_per_cta = threads / 32;
   const uint32_t grid = (p.n + warps_per_cta - 1) / warps_per_cta;
   index_lookup_kernel<<<grid, threads, 0, stream>>>(p);
