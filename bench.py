@@ -73,6 +73,9 @@ def parse() -> argparse.Namespace:
                     help="profiling case: 16 layers, 512-block pool, 64 blocks per step (same kernels)")
     ap.add_argument("--parallelism", choices=["sharded", "independent"], default="sharded",
                     help="N > 1: one hash-sharded store over all GPUs (default) or an independent store per GPU")
+    ap.add_argument("--placement", choices=["d2h", "uniform"], default="d2h",
+                    help="N > 1: place keys in proportion to each GPU's device->host rate measured while all "
+                         "copy at once (the write-through bound; default) or uniformly (fnv1a32 mod N)")
     ap.add_argument("--transport", choices=["p2p", "nccl"], default="p2p",
                     help="sharded store: P2P stores over NVLink (default) or NCCL send/recv of packed values")
     ap.add_argument("--mix", action="store_true",
@@ -441,6 +444,18 @@ def _host_write_rates(torch, dist, device, chunks=128, chunk=16 << 20):
     return best, -float(lo.item()), float(tot.item())
 
 
+def _placement_weights(torch, dist, device):
+    """Every rank's device->host rate while all ranks copy at once, clipped to [0.5, 1.5] x the mean:
+    the write-through each shard can absorb per second, used as its share of the keys."""
+    mine, _, _ = _host_write_rates(torch, dist, device)
+    t = torch.zeros(dist.get_world_size(), dtype=torch.float64, device=device)
+    t[dist.get_rank()] = mine
+    dist.all_reduce(t)
+    rates = t.cpu().numpy()
+    clipped = np.clip(rates, 0.5 * rates.mean(), 1.5 * rates.mean())
+    return [round(float(x), 3) for x in rates], [round(float(x), 3) for x in clipped]
+
+
 def _nvlink_roofline(torch, dist, device, timing, counters0, counters1, payload):
     """Per launch: the payload bytes that crossed NVLink / the launch's device time, for the client
     put kernel (P2P stores into the owners' slabs) and the owner get kernel (P2P stores into the
@@ -479,9 +494,14 @@ def run_sharded(args, rank, local_rank, world):
     block_units = 1 << (units - 1).bit_length()
     slab_values = 3 * BATCH_BLOCKS
     max_keys = 4 * BATCH_BLOCKS
+    rates, weights = _placement_weights(torch, dist, device) if args.placement == "d2h" else (None, None)
+    # with weights within [0.5, 1.5] x their mean a shard takes at most 192 / 256 / 307 puts per step
+    # at N = 2 / 4 / 8, which fit the 384 slab values and 512 catalog slots once the previous step's
+    # blocks, served at the start of the step, make room
     store = sharded.create(layout, max_batch=BATCH_BLOCKS, transport=args.transport, max_keys=max_keys,
                            heap_bytes=slab_values * block_units * UNIT_BYTES,
-                           host_pool_bytes=(max_keys + 8) * units * UNIT_BYTES, max_value_bytes=64 << 20)
+                           host_pool_bytes=(max_keys + 8) * units * UNIT_BYTES, max_value_bytes=64 << 20,
+                           weights=weights)
     eng = store.engine
     rng = np.random.default_rng(1000 + rank)
     lib = _native.load()
@@ -596,6 +616,9 @@ def run_sharded(args, rank, local_rank, world):
             "l2": f"inputs larger than L2 ({BATCH_BLOCKS * BLOCK_PAYLOAD / 2**30:.2f} GiB per direction per rank per step)",
             "parallelism": f"hash-sharded store over {world} GPUs, transport {args.transport}",
             "slab_bytes": slab_values * block_units * UNIT_BYTES,
+            "placement": ({"by": "each GPU's device->host rate while all copy at once (GB/s), clipped to "
+                                 "[0.5, 1.5] x the mean; keys go to fnv1a32 slots in proportion",
+                           "rates": rates, "weights": weights} if weights else {"by": "fnv1a32 mod N"}),
         },
         "e2e": {"value": round(e2e, 3), "unit": UNIT,
                 "h2d_bytes_per_step": 2 * 8 * world * sharded.request_words(BATCH_BLOCKS),

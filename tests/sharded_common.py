@@ -55,16 +55,16 @@ def make_pools(world: int, n_members: int, member_bytes: int, n_pool: int, seed:
             for _ in range(world)]
 
 
-def replay(plan, pools, member_bytes, store_cfg, n_shards: int | None = None):
+def replay(plan, pools, member_bytes, store_cfg, n_shards: int | None = None, table=None):
     """Expected result: (final pools, found flags [step][rank], per-shard stats). n_shards defaults
-    to one shard per rank."""
+    to one shard per rank; `table` is the store's key placement table (None: fnv1a32 mod n)."""
     found = []
-    for pools_now, f_row, stats in replay_steps(plan, pools, member_bytes, store_cfg, n_shards):
+    for pools_now, f_row, stats in replay_steps(plan, pools, member_bytes, store_cfg, n_shards, table):
         found.append(f_row)
     return pools_now, found, stats
 
 
-def replay_steps(plan, pools, member_bytes, store_cfg, n_shards: int | None = None):
+def replay_steps(plan, pools, member_bytes, store_cfg, n_shards: int | None = None, table=None):
     """The replay one step at a time: yields (pools, found flags per rank, per-shard stats) after
     every step; the stats of the last step follow a final flush."""
     world = len(pools)
@@ -77,13 +77,13 @@ def replay_steps(plan, pools, member_bytes, store_cfg, n_shards: int | None = No
         for o in range(n_shards):
             for s in range(world):
                 gk, gi = row[s][0], row[s][1]
-                sel = np.flatnonzero(shard_of_u64(gk, n_shards) == o)
+                sel = np.flatnonzero(shard_of_u64(gk, n_shards, table) == o)
                 if sel.size:
                     f_row[s][sel] = stores[o].get_blocks(pools[s], mb, gk[sel], gi[sel])
         for o in range(n_shards):
             for s in range(world):
                 pk, pi = row[s][2], row[s][3]
-                sel = np.flatnonzero(shard_of_u64(pk, n_shards) == o)
+                sel = np.flatnonzero(shard_of_u64(pk, n_shards, table) == o)
                 if sel.size:
                     stores[o].put_blocks(pools[s], mb, pk[sel], pi[sel])
         if step == len(plan) - 1:

@@ -27,14 +27,14 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, steps, batch, grant_limit, q):
+def _worker(rank, world, port, steps, batch, grant_limit, q, weights=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         plan = make_plan(world, steps, N_POOL, batch, seed=11)
         pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=3)
         eng = HostEngine(pools[rank], MB, CFG, grant_limit=grant_limit)
-        store = sharded.ShardedStore(eng, max_batch=batch, transport="nccl")
+        store = sharded.ShardedStore(eng, max_batch=batch, transport="nccl", weights=weights)
         found = []
         for row in plan:
             gk, gi, pk, pi = row[rank]
@@ -75,6 +75,47 @@ def test_sharded_protocol_matches_per_shard_oracle(world, grant_limit):
         if grant_limit:
             assert rounds > steps  # some steps took more than one grant round
     assert any(f.any() for fs in exp_found for f in fs) and not all(f.all() for fs in exp_found for f in fs)
+
+
+def test_weighted_placement_matches_per_shard_oracle():
+    """Keys placed in proportion to per-shard weights (as by each GPU's device->host rate): the
+    shards own their share of the keys and every rank's results equal the oracle replay with the
+    same placement."""
+    world, steps, batch, weights = 3, 5, 12, [1.0, 2.5, 1.5]
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, steps, batch, None, q, weights)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = sorted((q.get(timeout=240) for _ in range(world)), key=lambda o: o[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    table = sharded.placement_table(weights)
+    plan = make_plan(world, steps, N_POOL, batch, seed=11)
+    pools = make_pools(world, N_MEMBERS, MB, N_POOL, seed=3)
+    exp_pools, exp_found, exp_stats = replay(plan, pools, MB, CFG, table=table)
+    for rank, members, found, stats, ex, rounds in out:
+        for m in range(N_MEMBERS):
+            assert np.array_equal(members[m], exp_pools[rank][m]), f"rank {rank} member {m}"
+        for s in range(steps):
+            assert np.array_equal(found[s], exp_found[s][rank]), f"rank {rank} step {s}"
+        assert stats["live_keys"] == exp_stats[rank]["live_keys"]
+    keys = np.random.default_rng(0).integers(0, 2**63, 30000).astype(np.uint64)
+    share = np.bincount(sharded.shard_of_u64(keys, world, table), minlength=world) / keys.size
+    assert np.allclose(share, np.array(weights) / sum(weights), atol=0.02)
+
+
+def test_placement_table_shares():
+    for w in ([1, 1], [1, 2, 3], [11.5] * 4 + [18.2] * 4, [3.0]):
+        t = sharded.placement_table(w)
+        assert t.size == sharded.PLACEMENT_SLOTS and (np.diff(t) >= 0).all()
+        counts = np.bincount(t, minlength=len(w))
+        assert np.all(np.abs(counts - np.array(w) / sum(w) * sharded.PLACEMENT_SLOTS) < 1)
+    for bad in ([], [1, 0], [1, -2], [float("nan")]):
+        with pytest.raises(ValueError):
+            sharded.placement_table(bad)
 
 
 def test_pack_unpack_requests_round_trip():

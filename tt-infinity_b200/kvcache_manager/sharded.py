@@ -40,18 +40,44 @@ from ._native import KvsError, check, load
 _HDR = 4  # words at the head of every record
 
 
-def shard_of_u64(keys: np.ndarray, n_shards: int) -> np.ndarray:
-    """Owning shard of each 64-bit key: fnv1a32 of its 8 little-endian bytes, mod n_shards."""
+PLACEMENT_SLOTS = 4096
+
+
+def fnv1a32_u64(keys: np.ndarray) -> np.ndarray:
+    """fnv1a32 of each 64-bit key's 8 little-endian bytes (the hash the C ABI shards by)."""
     keys = np.ascontiguousarray(np.asarray(keys, dtype=np.uint64))
-    if n_shards == 1:
-        return np.zeros(keys.size, np.int64)
     b = keys.astype("<u8").view(np.uint8).reshape(-1, 8)
     h = np.full(keys.size, 2166136261, np.uint32)
     prime = np.uint32(16777619)
     for j in range(8):
         h ^= b[:, j]
         h *= prime
-    return (h % np.uint32(n_shards)).astype(np.int64)
+    return h
+
+
+def placement_table(weights: Sequence[float]) -> np.ndarray:
+    """Shard of each of PLACEMENT_SLOTS hash slots: contiguous slot ranges sized in proportion to
+    the weights (largest remainder, ties to the lower shard), so shard s owns about
+    weights[s] / sum(weights) of the keys."""
+    w = np.asarray(weights, dtype=np.float64)
+    if w.ndim != 1 or w.size == 0 or not np.all(np.isfinite(w)) or np.any(w <= 0):
+        raise ValueError("placement weights must be positive and finite, one per shard")
+    q = w / w.sum() * PLACEMENT_SLOTS
+    n = np.floor(q).astype(np.int64)
+    order = np.argsort(-(q - n), kind="stable")
+    n[order[:PLACEMENT_SLOTS - int(n.sum())]] += 1
+    return np.repeat(np.arange(w.size, dtype=np.int64), n)
+
+
+def shard_of_u64(keys: np.ndarray, n_shards: int, table: np.ndarray | None = None) -> np.ndarray:
+    """Owning shard of each 64-bit key: fnv1a32 of its 8 little-endian bytes mod n_shards, or,
+    with a placement table, the table's shard for slot fnv1a32 mod PLACEMENT_SLOTS."""
+    keys = np.ascontiguousarray(np.asarray(keys, dtype=np.uint64))
+    if table is not None:
+        return table[fnv1a32_u64(keys) % np.uint32(PLACEMENT_SLOTS)]
+    if n_shards == 1:
+        return np.zeros(keys.size, np.int64)
+    return (fnv1a32_u64(keys) % np.uint32(n_shards)).astype(np.int64)
 
 
 def request_words(cap: int) -> int:
@@ -65,12 +91,13 @@ def reply_words(cap: int) -> int:
 
 
 def pack_requests(world: int, cap: int, op: int, get_keys: np.ndarray, get_ids: np.ndarray,
-                  put_keys: np.ndarray, put_ids: np.ndarray) -> tuple[np.ndarray, list, list]:
+                  put_keys: np.ndarray, put_ids: np.ndarray,
+                  table: np.ndarray | None = None) -> tuple[np.ndarray, list, list]:
     """Request records [world, request_words(cap)] (record o goes to shard o) and, per owner, the
     batch positions of its gets and of its puts (in batch order)."""
     rec = np.zeros((world, request_words(cap)), np.int64)
-    g_own = shard_of_u64(get_keys, world)
-    p_own = shard_of_u64(put_keys, world)
+    g_own = shard_of_u64(get_keys, world, table)
+    p_own = shard_of_u64(put_keys, world, table)
     g_pos, p_pos = [], []
     gk = np.asarray(get_keys, np.uint64).view(np.int64)
     pk = np.asarray(put_keys, np.uint64).view(np.int64)
@@ -274,7 +301,8 @@ class ShardedStore:
     block bytes with copy kernels over NVLink peer memory; "nccl" moves contiguous rows with
     NCCL send/recv (the comparison transport)."""
 
-    def __init__(self, engine: Any, *, max_batch: int = 256, transport: str = "p2p", group=None) -> None:
+    def __init__(self, engine: Any, *, max_batch: int = 256, transport: str = "p2p", group=None,
+                 weights: Sequence[float] | None = None) -> None:
         import torch
         import torch.distributed as dist
 
@@ -284,6 +312,18 @@ class ShardedStore:
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        # key placement: fnv1a32 mod world, or slots in proportion to per-shard weights (the same
+        # on every rank, e.g. each GPU's device->host rate, which bounds its write-through)
+        self.table = None
+        if weights is not None:
+            w = [float(x) for x in weights]
+            if len(w) != self.world:
+                raise ValueError(f"sharded store: {len(w)} placement weights for {self.world} shards")
+            seen: list = [None] * self.world
+            dist.all_gather_object(seen, w, group=group)
+            if any(x != w for x in seen):
+                raise ValueError("sharded store: placement weights differ between ranks")
+            self.table = placement_table(w)
         self.engine = engine
         self.engine._rank = self.rank
         self.cap = int(max_batch)
@@ -369,7 +409,7 @@ class ShardedStore:
         if self.closed:
             raise KvsError(_native.E_CLOSED, "sharded store is closed")
         world, cap, eng = self.world, self.cap, self.engine
-        send, g_pos, p_pos = pack_requests(world, cap, 0, gk, gi, pk, pi)
+        send, g_pos, p_pos = pack_requests(world, cap, 0, gk, gi, pk, pi, self.table)
         reqs = unpack_requests(self._alltoall(send), cap)
         # ---- owner: gets of every source, in source-rank order
         n_get = [r[0].size for r in reqs]
@@ -498,7 +538,7 @@ class ShardedStore:
         k = np.ascontiguousarray(np.asarray(keys, dtype=np.uint64).reshape(-1))
         world, cap = self.world, self.cap
         send, g_pos, _ = pack_requests(world, cap, 1, k, np.zeros(k.size, np.int64), np.zeros(0, np.uint64),
-                                       np.zeros(0, np.int64))
+                                       np.zeros(0, np.int64), self.table)
         reqs = unpack_requests(self._alltoall(send), cap)
         n = [r[0].size for r in reqs]
         keys_all = np.concatenate([r[0] for r in reqs]) if sum(n) else np.zeros(0, np.uint64)
@@ -534,6 +574,7 @@ class ShardedStore:
 
 
 def create(layout: PagedLayout, *, max_batch: int = 256, transport: str = "p2p", group=None,
-           **server_cfg: Any) -> ShardedStore:
+           weights: Sequence[float] | None = None, **server_cfg: Any) -> ShardedStore:
     """A sharded store whose shard on this rank lives on the layout's GPU (collective)."""
-    return ShardedStore(DeviceEngine(layout, **server_cfg), max_batch=max_batch, transport=transport, group=group)
+    return ShardedStore(DeviceEngine(layout, **server_cfg), max_batch=max_batch, transport=transport, group=group,
+                        weights=weights)
