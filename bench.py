@@ -638,8 +638,10 @@ def run_sharded(args, rank, local_rank, world):
             "concurrent_d2h_GBps_per_gpu": {"rank0": round(hw_mine, 2), "min": round(hw_min, 2)},
             "concurrent_d2h_GBps_all_gpus": round(hw_sum, 1),
             "frac_of_slowest_gpu": round(wt_per_gpu / hw_min, 4),
+            "frac_of_box_aggregate": round(world * wt_per_gpu / hw_sum, 4),
             "note": ("every put is written through to the owner's pinned host tier and the next step's gets wait "
-                     "for it: the step is bound by the slowest GPU's device->host rate while all GPUs copy at once"),
+                     "for it: with equal key shares the step is bound by the slowest GPU's device->host rate "
+                     "while all GPUs copy at once; with shares by rate, by the box's aggregate rate"),
         },
         "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
                                      "samples": len(lat), "note": "one collective step, every rank gets one block"},
