@@ -820,10 +820,10 @@ int flush_puts(PutBatch &b, cudaStream_t) {
       p.tiles_per_combo = b.fmt->tile_prefix.back();
       p.total_tiles = (uint64_t)n * p.tiles_per_combo;
       p.to_blob = 1;
-      cudaEvent_t t0 = nullptr;
-      c->time_begin(&t0);
+      cudaEvent_t timed_start = nullptr;
+      c->time_begin(&timed_start);
       CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
-      c->time_end(t0, 0, (uint64_t)n * (b.fmt->value_len - 4ull * b.fmt->header.size()));
+      c->time_end(timed_start, 0, (uint64_t)n * (b.fmt->value_len - 4ull * b.fmt->header.size()));
     } else {
       for (size_t i = 0; i < n; ++i) {
         const size_t r = blobs_off + 48 * i;
