@@ -94,6 +94,35 @@ def test_null_and_invalid_arguments_fail_without_a_device(lib):
     assert b"header must be 32-byte aligned" in lib.kvs_last_error()
 
 
+def test_more_entry_points_validate_before_any_device_access(lib):
+    P = C.c_void_p
+    arr = (P * 1)(P(1))
+    # paged fill: nothing to do for zero layers, then argument checks in the reference's order
+    assert lib.kvs_paged_fill_varlen_layers(0, None, None, 1, 32, 64, None, 1, None, 1, None, None, None, 4, 16,
+                                            None, None) == 0
+    assert lib.kvs_paged_fill_varlen_layers(1, None, arr, 1, 32, 64, None, 1, None, 1, None, arr, arr, 4, 16,
+                                            None, None) == _native.E_INVAL
+    assert b"layer arrays are null" in lib.kvs_last_error()
+    assert lib.kvs_paged_fill_varlen_layers(1, arr, arr, 1, 32, 64, None, 0, None, 1, None, arr, arr, 4, 16,
+                                            None, None) == _native.E_INVAL
+    assert b"at least one row" in lib.kvs_last_error()
+    assert lib.kvs_paged_fill_varlen(P(1), P(1), 1, 32, 64, None, 1, None, 8, None, P(1), P(1), 4, 16, None,
+                                     None) == _native.E_INVAL
+    assert b"must be <= max_num_blocks" in lib.kvs_last_error()
+    assert lib.kvs_paged_fill_varlen(P(1), P(1), 1, 32, 64, None, 1, None, 1, None, P(1), P(1), 4, 0, None,
+                                     None) == _native.E_INVAL
+    assert b"must be > 0" in lib.kvs_last_error()
+    # batch limits and null handles
+    assert lib.kvs_put_batch(None, 129, None, None, None, None, 0, None) == _native.E_INVAL
+    assert b"128-descriptor limit" in lib.kvs_last_error()
+    found = (C.c_uint8 * 1)()
+    assert lib.kvs_get_parallel(None, 0, None, None, P(1), 0, 1, found, None) == _native.E_INVAL
+    h = _native.IpcHandle()
+    off = C.c_uint64()
+    assert lib.kvs_ipc_export(None, C.byref(h), C.byref(off)) == _native.E_INVAL
+    assert lib.kvs_ipc_open(0, None, None) == _native.E_INVAL
+
+
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(ImportError, match="requires its native extension"):
         _native.load(tmp_path / "libkvs_b200.so")
