@@ -317,10 +317,14 @@ int kvs_scatter_chunk(const void *blob, uint64_t blob_bytes, const uint64_t *mem
  * nearly all HBM to their paged KV pool and leave no headroom (or must keep their memory
  * accounting exact), and latency-critical restore paths where an allocation could synchronise
  * the device.
+ *   - The metadata reaches the array in the parameters of small staging kernels queued ahead of
+ *     the copy (no host-to-device memory copy), so the calling thread never waits for earlier
+ *     work on the stream.
  *   - Limit: the metadata must fit KVS_NOALLOC_SCRATCH_BYTES (8 x n_ranks x n_members
  *     + 24 x n_members + 8 x n_blocks + 4 x n_header_words bytes, each part rounded up to 16,
  *     about 64 KiB); larger requests fail with KVS_E_INVAL and a message naming the limit.
  *   - Every GPU that loads the library holds the array (64 KiB) until the process exits.
+ *   - A copy whose bounded waits expired shows only in kvs_copy_engine_status.
  *   - The first call on a device looks up the array's device address; make that first call
  *     before any stream capture on that device.
  *   - All calls share the array and each call overwrites it: calls whose work overlaps on the
@@ -337,6 +341,29 @@ int kvs_gather_chunk_noalloc(const uint64_t *member_ptrs, uint32_t n_ranks, uint
 /* kernels launched by this library since load (a launch counter for the benchmark) */
 uint64_t kvs_kernel_launch_count(void);
 
+/* ---- copy-engine health ----
+ * Every wait of the bulk-copy engine on a tile load is bounded (the reference's device runtime
+ * bounds its NoC waits the same way and reports a timeout instead of hanging). A wait that expires
+ * stops its CTA's copy early: the CTA first lets every load it issued land (each with the full
+ * limit), then exits, and the result is incomplete.
+ *   - Store calls report it themselves: the next call that synchronises (get, get_blocks, exists,
+ *     flush, a sync_commit put) returns KVS_E_TIMEOUT and quarantines the client, so every later
+ *     call returns KVS_E_QUARANTINED (the reference's Quarantined state,
+ *     src/client_operations_adapter.cpp:54-59).
+ *   - The asynchronous chunk ops (kvs_gather_chunk, kvs_scatter_chunk, kvs_gather_chunk_noalloc)
+ *     return before their kernel runs, so they report it only here: after synchronising the stream,
+ *     a count that grew since the last read means the blobs or blocks of the calls in between are
+ *     incomplete.
+ * expired_waits: waits on `device` that expired since the library loaded. unsafe_exits: CTAs that
+ * exited while a load of theirs still had not landed after the full limit (never seen in normal
+ * operation; the engine on that device cannot be trusted afterwards). No counterpart in the
+ * reference. */
+int kvs_copy_engine_status(int32_t device, uint32_t *expired_waits, uint32_t *unsafe_exits);
+/* Polls of each bounded tile-load wait for launches from now on, process-wide; a negative value
+ * restores the default (2^22 polls). Tests of the expiry path pass 0, which expires a CTA's first
+ * wait at once while its loads still land normally. No counterpart in the reference. */
+int kvs_set_copy_wait_limit(int64_t polls);
+
 /* Per-client kernel timing: with timing on, CUDA events bracket every gather (put) and scatter
  * (get) copy-engine launch on the client stream. kvs_client_timing waits for them, returns the
  * totals since the last call (and resets). bytes = payload bytes the kernels moved. */
@@ -347,6 +374,19 @@ typedef struct {
 } kvs_kernel_timing;
 int kvs_client_set_timing(kvs_client *c, int enable);
 int kvs_client_timing(kvs_client *c, kvs_kernel_timing *gather, kvs_kernel_timing *scatter);
+/* The same for the host-tier copies of a get (timing on): admissions = copy launches that read
+ * host-tier values over PCIe into their new slab blocks (bytes = whole values), serves = copy
+ * launches that scatter host-tier hits into the paged pool (bytes = payload), from the slab block
+ * their admission filled or, when no block could be allocated, from the pinned host copy. No
+ * counterpart in the reference. */
+int kvs_client_host_tier_timing(kvs_client *c, kvs_kernel_timing *admissions, kvs_kernel_timing *serves);
+/* Per-shard write-through timing: with timing on, CUDA events on the shard's write-through stream
+ * bracket each batch of device->host copies (one batch per put call). kvs_server_write_through_timing
+ * waits for them and returns the totals since the last call (and resets): launches = batches,
+ * bytes = bytes copied to the host tier, total_ms = the copies' device time. No counterpart in the
+ * reference (its tiering thread keeps MoveProfile wall-clock totals, kvs_server_move_profile). */
+int kvs_server_set_timing(kvs_server *s, int enable);
+int kvs_server_write_through_timing(kvs_server *s, kvs_kernel_timing *out);
 
 #ifdef __cplusplus
 }

@@ -130,7 +130,10 @@ constexpr uint32_t kTmaTile = 32u << 10;
 constexpr size_t kTmaSmem = (size_t)kTmaStages * kTmaTile;
 constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier waits (seconds at most), then give up
 
+std::atomic<uint32_t> g_wait_polls{kSpinLimit};
+
 __device__ unsigned int g_tma_timeouts = 0;  // read by the host after a synchronising call
+__device__ unsigned int g_tma_unsafe = 0;    // CTAs that exited with a load still in flight
 
 struct TileRef {
   uint8_t *member;
@@ -153,8 +156,8 @@ __device__ __forceinline__ void bulk_wait_read(int allowed) {
   }
 }
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t spin = 0; spin < kSpinLimit; ++spin) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t polls) {
+  for (uint32_t spin = 0; spin < polls; ++spin) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
@@ -319,13 +322,18 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const __gri
     if (k_done == k_load) break;
     const int stage = (int)(k_done % kTmaStages);
     const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&full_bar[stage]);
-    if (!mbar_wait(bar, (uint32_t)((k_done / kTmaStages) & 1))) {
+    if (!mbar_wait(bar, (uint32_t)((k_done / kTmaStages) & 1), p.wait_polls)) {
       atomicAdd(&g_tma_timeouts, 1u);
       if (p.timeout_flag) *reinterpret_cast<volatile unsigned int *>(p.timeout_flag) = 1u;
       failed = true;
-      // give the loads still in flight a bounded chance to land before the CTA exits
-      for (uint64_t j = k_done + 1; j < k_load; ++j)
-        mbar_wait((uint32_t)__cvta_generic_to_shared(&full_bar[j % kTmaStages]), (uint32_t)((j / kTmaStages) & 1));
+      // Loads k_done .. k_load-1 were issued and still write into this CTA's shared memory (the
+      // one that just expired included): the CTA must not exit before they land. Each gets the
+      // full wait limit, whatever limit the expired wait had; one that still has not landed is
+      // counted as an unsafe exit, which the host reports as an engine it cannot trust.
+      for (uint64_t j = k_done; j < k_load; ++j)
+        if (!mbar_wait((uint32_t)__cvta_generic_to_shared(&full_bar[j % kTmaStages]),
+                       (uint32_t)((j / kTmaStages) & 1), kSpinLimit))
+          atomicAdd(&g_tma_unsafe, 1u);
       break;
     }
     const TileRef &rd = ring[stage];
@@ -685,14 +693,21 @@ cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream)
   uint64_t grid = (uint64_t)sm_count();
   if (grid > p.total_tiles && p.total_tiles > 0) grid = p.total_tiles;
   if (grid == 0) grid = 1;
-  chunk_copy_tma_kernel<<<(unsigned)grid, kTmaThreads, kTmaSmem, stream>>>(p);
+  ChunkCopyParams q = p;
+  q.wait_polls = g_wait_polls.load(std::memory_order_relaxed);
+  chunk_copy_tma_kernel<<<(unsigned)grid, kTmaThreads, kTmaSmem, stream>>>(q);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }
 
-cudaError_t read_tma_timeouts(unsigned int *count) {
-  return cudaMemcpyFromSymbol(count, g_tma_timeouts, sizeof(unsigned int));
+cudaError_t read_tma_counters(unsigned int *expired, unsigned int *unsafe) {
+  cudaError_t e = cudaMemcpyFromSymbol(expired, g_tma_timeouts, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(unsafe, g_tma_unsafe, sizeof(unsigned int));
+  return e;
 }
+
+void set_copy_wait_polls(uint32_t polls) { g_wait_polls.store(polls, std::memory_order_relaxed); }
+uint32_t default_copy_wait_polls() { return kSpinLimit; }
 
 cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream) {
   if (p.n == 0) return cudaSuccess;

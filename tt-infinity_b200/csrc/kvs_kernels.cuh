@@ -76,6 +76,7 @@ struct ChunkCopyParams {
   uint64_t total_tiles;
   int to_blob;               // 1: members -> blob (gather), 0: blob -> members (scatter)
   unsigned int *timeout_flag;  // optional host-mapped word set to 1 if a bounded wait expires
+  uint32_t wait_polls;       // polls of one bounded wait on a tile load (set by the launcher)
   int64_t inline_ids[kInlineKeys];  // block ids when block_ids is nullptr (n_blobs * blocks_per_blob <= 8)
 };
 
@@ -134,8 +135,15 @@ struct FillLayers {  // by value in the kernel parameters (2 KiB)
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas = 0);
 // TMA bulk-copy variant (sources and destinations in device memory, this GPU's or a peer's).
 cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream);
-// Bounded-wait expiries of the bulk-copy engine on the current device (0 in normal operation).
-cudaError_t read_tma_timeouts(unsigned int *count);
+// Counters of the bulk-copy engine on the current device (both 0 in normal operation): bounded
+// waits on a tile load that expired, and CTAs that exited while one of their loads still had not
+// landed after the full wait limit (the engine cannot be trusted after that).
+cudaError_t read_tma_counters(unsigned int *expired, unsigned int *unsafe);
+// Polls of the bulk-copy engine's bounded wait on each tile load for launches from now on (0
+// expires every wait at once; a test of the expiry path uses it). default_copy_wait_polls() is
+// the production limit.
+void set_copy_wait_polls(uint32_t polls);
+uint32_t default_copy_wait_polls();
 cudaError_t launch_index_lookup(const LookupParams &p, cudaStream_t stream);
 cudaError_t launch_apply_mutations(const MutationParams &p, cudaStream_t stream);
 cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &layers, uint32_t n_layers,

@@ -5,9 +5,15 @@
 // allow that: a serving engine that has handed nearly all of HBM to its paged KV pool has no
 // headroom for another allocation (and must not have its memory accounting disturbed), and a
 // latency-critical restore path cannot afford cudaMalloc / cudaFree, which may synchronise the
-// device. This entry point stages the same metadata in one fixed device array that lives in this
+// device. This entry point keeps the same metadata in one fixed device array that lives in this
 // file instead, so it never calls cudaMalloc, cudaMallocAsync, cudaFree or any allocating library
 // routine. Every GPU that loads the library holds that array (kNoAllocScratchBytes) until exit.
+//
+// The metadata reaches the array without any host-to-device memory copy: it travels by value in
+// the parameters of small staging kernels (up to kParamChunkBytes per launch), which write it into
+// the array in stream order ahead of the copy kernel. Kernel parameters are captured when the
+// launch is queued, so the host-side image is free for the next call as soon as this call returns,
+// and the calling thread never waits for earlier work on the stream.
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -16,22 +22,44 @@
 #include <mutex>
 
 #include "kvs.h"
+#include "kvs_chunk_meta.hpp"
 #include "kvs_kernels.cuh"
 
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = KVS_NOALLOC_SCRATCH_BYTES;
-constexpr uint32_t kNoAllocTileBytes = 32u << 10;
 constexpr int kMaxDevices = 64;
 
 // Shared by every call on a device; each call overwrites the part it uses before its kernel reads
 // it. Nothing in it needs to start at zero.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
+// One staging launch carries this many metadata bytes in its parameters (kernel parameters may
+// take up to 32764 bytes).
+constexpr uint32_t kParamChunkBytes = 30u << 10;
+struct alignas(16) StageChunk {
+  uint32_t offset;  // destination offset inside the scratch array (16-byte aligned)
+  uint32_t bytes;   // multiple of 16
+  uint32_t pad[2];
+  uint8_t data[kParamChunkBytes];
+};
+static_assert(sizeof(StageChunk) <= 32764, "staging parameters exceed the kernel parameter limit");
+
+__global__ void stage_meta_kernel(const __grid_constant__ StageChunk c) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(c.data);
+  uint4 *dst = reinterpret_cast<uint4 *>(g_noalloc_scratch + c.offset);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < c.bytes / 16; i += gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
 std::mutex g_setup_mu;
 void *g_scratch_addr[kMaxDevices] = {};  // device address of g_noalloc_scratch, per device
 
-thread_local uint8_t g_host_image[kNoAllocScratchBytes];  // host-side image of one call's metadata
+// Host-side buffers of one call (static, so a call allocates nothing on the host either); a call
+// holds g_image_mu while it packs them and queues its launches, which capture their parameters.
+std::mutex g_image_mu;
+uint8_t g_host_image[kNoAllocScratchBytes];  // one call's metadata, packed on the host
+StageChunk g_chunk;                          // parameters of one staging launch
 
 int fail(int code, const char *fmt, ...) {
   char buf[512];
@@ -60,7 +88,21 @@ int scratch_address(int device, uint8_t **out) {
   return KVS_OK;
 }
 
-size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+// Writes image[0, bytes) into the scratch array in stream order, kParamChunkBytes per launch.
+cudaError_t stage_image(const uint8_t *image, size_t bytes, cudaStream_t stream) {
+  for (size_t off = 0; off < bytes; off += kParamChunkBytes) {
+    const uint32_t n = (uint32_t)(bytes - off < kParamChunkBytes ? bytes - off : kParamChunkBytes);
+    g_chunk.offset = (uint32_t)off;
+    g_chunk.bytes = n;
+    std::memcpy(g_chunk.data, image + off, n);
+    const uint32_t words = n / 16;
+    const uint32_t grid = words / 256 + 1 < 8 ? words / 256 + 1 : 8;
+    stage_meta_kernel<<<grid, 256, 0, stream>>>(g_chunk);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
 
 }  // namespace
 
@@ -70,122 +112,35 @@ extern "C" int kvs_gather_chunk_noalloc(const uint64_t *member_ptrs, uint32_t n_
                                         const uint32_t *header_words, uint32_t n_header_words, void *blob,
                                         uint64_t blob_bytes, void *stream) {
   const char *op = "kvcache gather (no-alloc)";
-  if (n_ranks == 0) return fail(KVS_E_INVAL, "%s: rank_coords must not be empty", op);
-  if (n_members == 0) return fail(KVS_E_INVAL, "%s: members must not be empty", op);
-  if (n_blocks == 0) return fail(KVS_E_INVAL, "%s: block_ids must not be empty", op);
-  if (!member_ptrs || !member_block_bytes || !member_extent || !block_ids || !region_bases || !blob ||
-      (n_header_words && !header_words))
-    return fail(KVS_E_INVAL, "%s: null argument", op);
-  const uint64_t nrm = (uint64_t)n_ranks * n_members;
-  // scratch layout: member ptrs | block bytes | region bases | tile prefix | block ids | blob ptr | header
-  const size_t need = align16(8 * nrm) + 3 * align16(8ull * n_members + 8) + align16(8ull * n_blocks) + 16 +
-                      align16(4ull * n_header_words);
+  const size_t need = kvs::chunk_meta_bytes(n_ranks, n_members, n_blocks, n_header_words);
   if (need > kNoAllocScratchBytes)
     return fail(KVS_E_INVAL,
                 "%s: %u ranks x %u members, %u blocks and %u header words need %zu bytes of metadata, more than "
                 "the %zu-byte scratch; use kvs_gather_chunk",
                 op, n_ranks, n_members, n_blocks, n_header_words, need, kNoAllocScratchBytes);
-  const uint32_t header_bytes = 4 * n_header_words;
-  if (header_bytes % 32) return fail(KVS_E_INVAL, "%s: header must be 32-byte aligned, got %u B", op, header_bytes);
-  if (header_bytes > blob_bytes)
-    return fail(KVS_E_INVAL, "%s: %u B header exceeds the %llu B blob", op, header_bytes,
-                (unsigned long long)blob_bytes);
-  uint32_t max_block = 0;
-  for (uint32_t i = 0; i < n_blocks; ++i) max_block = max_block > block_ids[i] ? max_block : block_ids[i];
-  uint8_t *img = g_host_image;
-  size_t off = 0;
-  auto take = [&](size_t n) {
-    const size_t o = off;
-    off = align16(off + n);
-    return o;
-  };
-  const size_t o_mp = take(8 * nrm), o_mb = take(8ull * n_members + 8), o_rb = take(8ull * n_members + 8);
-  const size_t o_tp = take(8ull * n_members + 8), o_id = take(8ull * n_blocks), o_bl = take(8);
-  const size_t o_hw = take(4ull * n_header_words);
-  uint64_t *tile_prefix = reinterpret_cast<uint64_t *>(img + o_tp);
-  tile_prefix[0] = 0;
-  for (uint32_t m = 0; m < n_members; ++m) {
-    const uint64_t sbb = member_block_bytes[m];
-    if (sbb == 0 || sbb % 4)
-      return fail(KVS_E_INVAL, "%s: member %u block bytes %llu must be nonzero and 4-byte aligned", op, m,
-                  (unsigned long long)sbb);
-    if (region_bases[m] % 32)
-      return fail(KVS_E_INVAL, "%s: region base %llu must be 32-byte aligned", op, (unsigned long long)region_bases[m]);
-    if (region_bases[m] < header_bytes)
-      return fail(KVS_E_INVAL, "%s: member %u's region at %llu B overlaps the %u B header", op, m,
-                  (unsigned long long)region_bases[m], header_bytes);
-    if (((uint64_t)max_block + 1) * sbb > member_extent[m])
-      return fail(KVS_E_INVAL, "%s: block %u reaches past member %u's %llu B shard", op, max_block, m,
-                  (unsigned long long)member_extent[m]);
-    const uint64_t end = region_bases[m] + (uint64_t)n_blocks * sbb * n_ranks;
-    if (end > blob_bytes)
-      return fail(KVS_E_INVAL, "%s: member %u's region ends at %llu B, past the %llu B blob", op, m,
-                  (unsigned long long)end, (unsigned long long)blob_bytes);
-    tile_prefix[m + 1] = tile_prefix[m] + (sbb + kNoAllocTileBytes - 1) / kNoAllocTileBytes;
-  }
-  cudaPointerAttributes a{};
-  if (cudaPointerGetAttributes(&a, blob) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
-    cudaGetLastError();
-    return fail(KVS_E_INVAL, "%s: blob must be device memory", op);
-  }
+  const kvs::ChunkArgs a{member_ptrs, n_ranks,      n_members,    member_block_bytes, member_extent, block_ids,
+                         n_blocks,    region_bases, header_words, n_header_words,     blob,          blob_bytes,
+                         1};
+  kvs::ChunkMeta m{};
+  int rc = kvs::check_chunk_args(a, op, &m);
+  if (rc != KVS_OK) return rc;
   int prev = -1;
   cudaGetDevice(&prev);
-  if (prev != a.device) cudaSetDevice(a.device);
-  int rc = KVS_OK;
+  if (prev != m.device) cudaSetDevice(m.device);
   do {
-    for (uint64_t i = 0; i < nrm && rc == KVS_OK; ++i) {
-      cudaPointerAttributes ma{};
-      if (!member_ptrs[i] || cudaPointerGetAttributes(&ma, reinterpret_cast<const void *>(member_ptrs[i])) != cudaSuccess ||
-          ma.type != cudaMemoryTypeDevice) {
-        cudaGetLastError();
-        rc = fail(KVS_E_INVAL, "%s: member tensor must be device memory", op);
-      } else if (ma.device != a.device) {
-        const cudaError_t pe = cudaDeviceEnablePeerAccess(ma.device, 0);
-        if (pe == cudaErrorPeerAccessAlreadyEnabled)
-          cudaGetLastError();
-        else if (pe != cudaSuccess)
-          rc = fail(KVS_E_CUDA, "%s: enable peer access %d->%d: %s", op, a.device, ma.device, cudaGetErrorString(pe));
-      }
-    }
-    if (rc != KVS_OK) break;
     uint8_t *scratch = nullptr;
-    if ((rc = scratch_address(a.device, &scratch)) != KVS_OK) break;
-    std::memcpy(img + o_mp, member_ptrs, 8 * nrm);
-    std::memcpy(img + o_mb, member_block_bytes, 8ull * n_members);
-    std::memcpy(img + o_rb, region_bases, 8ull * n_members);
-    int64_t *ids = reinterpret_cast<int64_t *>(img + o_id);
-    for (uint32_t i = 0; i < n_blocks; ++i) ids[i] = block_ids[i];
-    const uint64_t blob_addr = reinterpret_cast<uint64_t>(blob);
-    std::memcpy(img + o_bl, &blob_addr, 8);
-    if (n_header_words) std::memcpy(img + o_hw, header_words, 4ull * n_header_words);
+    if ((rc = scratch_address(m.device, &scratch)) != KVS_OK) break;
+    std::lock_guard<std::mutex> lk(g_image_mu);
+    kvs::pack_chunk_meta(a, m, g_host_image);
     cudaStream_t s = (cudaStream_t)stream;
-    // a copy from pageable host memory returns once the image has been staged, so the host image
-    // can be reused by the next call
-    cudaError_t e = cudaMemcpyAsync(scratch, img, off, cudaMemcpyHostToDevice, s);
+    cudaError_t e = stage_image(g_host_image, m.bytes, s);
     if (e != cudaSuccess) {
-      rc = fail(KVS_E_CUDA, "%s: metadata upload: %s", op, cudaGetErrorString(e));
+      rc = fail(KVS_E_CUDA, "%s: metadata staging: %s", op, cudaGetErrorString(e));
       break;
     }
-    kvs::ChunkCopyParams p{};
-    p.member_ptrs = reinterpret_cast<const uint64_t *>(scratch + o_mp);
-    p.member_bytes = reinterpret_cast<const uint64_t *>(scratch + o_mb);
-    p.region_bases = reinterpret_cast<const uint64_t *>(scratch + o_rb);
-    p.tile_prefix = reinterpret_cast<const uint64_t *>(scratch + o_tp);
-    p.block_ids = reinterpret_cast<const int64_t *>(scratch + o_id);
-    p.blob_ptrs = reinterpret_cast<const uint64_t *>(scratch + o_bl);
-    p.header_words = reinterpret_cast<const uint32_t *>(scratch + o_hw);
-    p.n_header_words = n_header_words;
-    p.n_blobs = 1;
-    p.blocks_per_blob = n_blocks;
-    p.n_ranks = n_ranks;
-    p.n_members = n_members;
-    p.tile_bytes = kNoAllocTileBytes;
-    p.tiles_per_combo = tile_prefix[n_members];
-    p.total_tiles = (uint64_t)n_blocks * n_ranks * p.tiles_per_combo;
-    p.to_blob = 1;
-    e = kvs::launch_chunk_copy_tma(p, s);
+    e = kvs::launch_chunk(kvs::chunk_params(a, m, scratch), s);
     if (e != cudaSuccess) rc = fail(KVS_E_CUDA, "%s: launch: %s", op, cudaGetErrorString(e));
   } while (false);
-  if (prev >= 0 && prev != a.device) cudaSetDevice(prev);
+  if (prev >= 0 && prev != m.device) cudaSetDevice(prev);
   return rc;
 }

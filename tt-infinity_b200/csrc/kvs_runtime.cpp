@@ -31,6 +31,7 @@
 #include <vector>
 
 #include "kvs.h"
+#include "kvs_chunk_meta.hpp"
 #include "kvs_directory.hpp"
 #include "kvs_kernels.cuh"
 
@@ -367,15 +368,67 @@ struct kvs_server {
     }
     wt_runs.push_back({host, slab_ptr, len, len, len, 1});
   }
+  // Write-through timing (kvs_server_set_timing): events on the write-through stream around each
+  // batch of device->host copies, so the copies' own duration is measured, not inferred.
+  struct WtTimed {
+    cudaEvent_t start, stop;
+    uint64_t bytes;
+  };
+  bool wt_timing = false;
+  std::vector<WtTimed> wt_timed;
+  std::vector<cudaEvent_t> wt_timing_events;
+  kvs_kernel_timing wt_acc{};
+  cudaEvent_t timing_event() {
+    if (!wt_timing_events.empty()) {
+      cudaEvent_t e = wt_timing_events.back();
+      wt_timing_events.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    return e;
+  }
+  void drain_wt_timing() {
+    for (auto &t : wt_timed) {
+      float ms = 0.f;
+      if (cudaEventSynchronize(t.stop) == cudaSuccess && cudaEventElapsedTime(&ms, t.start, t.stop) == cudaSuccess) {
+        wt_acc.launches++;
+        wt_acc.bytes += t.bytes;
+        wt_acc.total_ms += ms;
+      } else {
+        cudaGetLastError();
+      }
+      wt_timing_events.push_back(t.start);
+      wt_timing_events.push_back(t.stop);
+    }
+    wt_timed.clear();
+  }
   int wt_issue() {
+    cudaEvent_t start = nullptr;
+    uint64_t bytes = 0;
+    if (wt_timing && !wt_runs.empty() && (start = timing_event()) != nullptr)
+      CUDA_TRY(cudaEventRecord(start, wt_stream));
     for (const WtRun &r : wt_runs) {
       if (r.n == 1)
         CUDA_TRY(cudaMemcpyAsync(r.host, r.slab, r.len, cudaMemcpyDeviceToHost, wt_stream));
       else
         CUDA_TRY(cudaMemcpy2DAsync(r.host, r.host_pitch, r.slab, r.slab_pitch, r.len, r.n, cudaMemcpyDeviceToHost,
                                    wt_stream));
+      bytes += r.len * r.n;
     }
     wt_runs.clear();
+    if (start) {
+      cudaEvent_t stop = timing_event();
+      if (!stop) {
+        wt_timing_events.push_back(start);
+        return KVS_OK;
+      }
+      CUDA_TRY(cudaEventRecord(stop, wt_stream));
+      wt_timed.push_back({start, stop, bytes});
+    }
     return KVS_OK;
   }
   // Commit the FIFO head, waiting for its device->host copy.
@@ -448,12 +501,12 @@ struct kvs_client {
   bool timing = false;
   struct Timed {
     cudaEvent_t start, stop;
-    int kind;  // 0 gather, 1 scatter
+    int kind;  // 0 gather, 1 scatter, 2 admission (host -> slab), 3 host-tier serve (host -> pool)
     uint64_t bytes;
   };
   std::vector<Timed> timed;
   std::vector<cudaEvent_t> event_pool;
-  kvs_kernel_timing acc[2]{};
+  kvs_kernel_timing acc[4]{};  // gather, scatter, host-tier admissions, host-tier serves
   cudaEvent_t pooled_event() {
     if (!event_pool.empty()) {
       cudaEvent_t e = event_pool.back();
@@ -495,13 +548,7 @@ namespace {
 
 // Copy-engine choice: the TMA bulk engine for device memory (this GPU's or a peer's), the
 // LDG/STG engine when a side is host memory. KVS_COPY_ENGINE=ldg forces the LDG engine.
-bool tma_enabled() {
-  static const bool on = [] {
-    const char *v = std::getenv("KVS_COPY_ENGINE");
-    return !(v && std::strcmp(v, "ldg") == 0);
-  }();
-  return on;
-}
+bool tma_enabled() { return kvs::bulk_engine_enabled(); }
 
 cudaError_t launch_copy(kvs::ChunkCopyParams p, cudaStream_t stream, bool device_memory_only,
                         unsigned int *timeout_flag) {
@@ -908,7 +955,8 @@ int stage_put(PutBatch &b, uint32_t si, const uint8_t *key, uint32_t key_len, ui
 int commit_barrier(kvs_client *c, const std::vector<uint8_t> &involved) {
   for (size_t i = 0; i < c->shards.size(); ++i)
     if (involved[i]) TRY(c->shards[i]->commit_all());
-  return KVS_OK;
+  // the write-through copies just waited for follow this client's gathers into those shards
+  return check_tma_timeouts(c, "commit");
 }
 
 std::vector<kvs_server *> involved_servers(kvs_client *c, const std::vector<uint8_t> &inv) {
@@ -919,7 +967,8 @@ std::vector<kvs_server *> involved_servers(kvs_client *c, const std::vector<uint
 }
 
 int quarantine_on_error(kvs_client *c, int rc) {
-  if (rc == KVS_E_CUDA && c) c->quarantined = true;
+  // a failed CUDA call or an expired copy-engine wait leaves the outcome indeterminate
+  if ((rc == KVS_E_CUDA || rc == KVS_E_TIMEOUT) && c) c->quarantined = true;
   return rc;
 }
 
@@ -976,6 +1025,25 @@ int kvs_abi_version(void) { return KVS_ABI_VERSION; }
 const char *kvs_last_error(void) { return g_err.c_str(); }
 
 uint64_t kvs_kernel_launch_count(void) { return kvs::kernel_launches(); }
+
+int kvs_copy_engine_status(int32_t device, uint32_t *expired_waits, uint32_t *unsafe_exits) {
+  if (!expired_waits || !unsafe_exits) return set_err(KVS_E_INVAL, "copy_engine_status: null output");
+  int ndev = 0;
+  CUDA_TRY(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return set_err(KVS_E_INVAL, "device %d is not a visible CUDA device", device);
+  DeviceGuard g(device);
+  unsigned int expired = 0, unsafe = 0;
+  CUDA_TRY(kvs::read_tma_counters(&expired, &unsafe));
+  *expired_waits = expired;
+  *unsafe_exits = unsafe;
+  return KVS_OK;
+}
+
+int kvs_set_copy_wait_limit(int64_t polls) {
+  if (polls > (int64_t)UINT32_MAX) return set_err(KVS_E_INVAL, "copy wait limit %lld exceeds 2^32 - 1 polls", (long long)polls);
+  kvs::set_copy_wait_polls(polls < 0 ? kvs::default_copy_wait_polls() : (uint32_t)polls);
+  return KVS_OK;
+}
 
 int kvs_server_config_default(kvs_server_config *cfg) {
   if (!cfg) return set_err(KVS_E_INVAL, "config is null");
@@ -1074,6 +1142,8 @@ int kvs_server_destroy(kvs_server *s) {
       if (!s->dir->fifo_empty()) rc = s->commit_all();
     }
     if (s->wt_stream) cudaStreamSynchronize(s->wt_stream);
+    s->drain_wt_timing();
+    for (auto e : s->wt_timing_events) cudaEventDestroy(e);
     for (auto &b : s->wt_batches) cudaEventDestroy(b.done);
     for (auto e : s->free_events) cudaEventDestroy(e);
     for (uint8_t *chunk : s->heap_chunks) cudaFreeHost(chunk);  // every off-pool value lives in one
@@ -1147,6 +1217,24 @@ int kvs_server_stats(kvs_server *s, kvs_stats *out) {
   out->issued = st.issued;
   out->committed = st.committed;
   out->kernel_launches = s->launches.load();
+  return KVS_OK;
+}
+
+int kvs_server_set_timing(kvs_server *s, int enable) {
+  if (!s) return set_err(KVS_E_INVAL, "server handle is null");
+  std::lock_guard<std::mutex> lk(s->mu);
+  DeviceGuard g(s->cfg.device);
+  s->wt_timing = enable != 0;
+  return KVS_OK;
+}
+
+int kvs_server_write_through_timing(kvs_server *s, kvs_kernel_timing *out) {
+  if (!s || !out) return set_err(KVS_E_INVAL, "server_write_through_timing: null argument");
+  std::lock_guard<std::mutex> lk(s->mu);
+  DeviceGuard g(s->cfg.device);
+  s->drain_wt_timing();
+  *out = s->wt_acc;
+  s->wt_acc = kvs_kernel_timing{};
   return KVS_OK;
 }
 
@@ -1989,7 +2077,10 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
       a.tiles_per_combo = adm_meta[3];
       a.total_tiles = (uint64_t)n_admit * a.tiles_per_combo;
       a.to_blob = 0;
+      cudaEvent_t ta = nullptr;
+      c->time_begin(&ta);
       CUDA_TRY(launch_copy(a, c->stream, false, c->timeout_flag));  // the source is host memory
+      c->time_end(ta, 2, (uint64_t)n_admit * fmt.value_len);
     }
     for (auto &L : late)
       if (L.admit_dst && !L.host_dev)  // no device alias: a copy-engine copy
@@ -2006,7 +2097,10 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
       q.blob_ptrs = st2.d<uint64_t>(blobs2);
       q.n_blobs = (uint32_t)nscatter;
       q.total_tiles = (uint64_t)nscatter * q.tiles_per_combo;
+      cudaEvent_t tq = nullptr;
+      c->time_begin(&tq);
       CUDA_TRY(launch_copy(q, c->stream, false, c->timeout_flag));
+      c->time_end(tq, 3, (uint64_t)nscatter * payload_per_block);
     }
     for (size_t i = 0; i < ns; ++i)
       if (inv[i]) TRY(chain_record(c, i));
@@ -2500,6 +2594,18 @@ int kvs_client_timing(kvs_client *c, kvs_kernel_timing *gather, kvs_kernel_timin
   return KVS_OK;
 }
 
+int kvs_client_host_tier_timing(kvs_client *c, kvs_kernel_timing *admissions, kvs_kernel_timing *serves) {
+  if (!c) return set_err(KVS_E_INVAL, "client handle is null");
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  c->drain_timing();
+  if (admissions) *admissions = c->acc[2];
+  if (serves) *serves = c->acc[3];
+  c->acc[2] = kvs_kernel_timing{};
+  c->acc[3] = kvs_kernel_timing{};
+  return KVS_OK;
+}
+
 // ---------------------------------------------------------------------------- chunk ops
 
 static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_members,
@@ -2507,109 +2613,22 @@ static int chunk_op(const uint64_t *member_ptrs, uint32_t n_ranks, uint32_t n_me
                     uint32_t n_blocks, const uint64_t *region_bases, const uint32_t *header_words,
                     uint32_t n_header_words, void *blob, uint64_t blob_bytes, void *stream, int to_blob,
                     const char *op) {
-  if (n_ranks == 0) return set_err(KVS_E_INVAL, "%s: rank_coords must not be empty", op);
-  if (n_members == 0) return set_err(KVS_E_INVAL, "%s: members must not be empty", op);
-  if (n_blocks == 0) return set_err(KVS_E_INVAL, "%s: block_ids must not be empty", op);
-  if (!member_ptrs || !member_block_bytes || !member_extent || !block_ids || !region_bases || !blob)
-    return set_err(KVS_E_INVAL, "%s: null argument", op);
-  const uint32_t header_bytes = 4 * n_header_words;
-  if (header_bytes % 32) return set_err(KVS_E_INVAL, "%s: header must be 32-byte aligned, got %u B", op, header_bytes);
-  if (header_bytes > blob_bytes)
-    return set_err(KVS_E_INVAL, "%s: %u B header exceeds the %llu B blob", op, header_bytes,
-                   (unsigned long long)blob_bytes);
-  uint32_t max_block = 0;
-  for (uint32_t i = 0; i < n_blocks; ++i) max_block = std::max(max_block, block_ids[i]);
-  std::vector<uint64_t> tile_prefix(n_members + 1, 0);
-  for (uint32_t m = 0; m < n_members; ++m) {
-    const uint64_t sbb = member_block_bytes[m];
-    if (sbb == 0 || sbb % 4)
-      return set_err(KVS_E_INVAL, "%s: member %u block bytes %llu must be nonzero and 4-byte aligned", op, m,
-                     (unsigned long long)sbb);
-    if (region_bases[m] % 32) return set_err(KVS_E_INVAL, "%s: region base %llu must be 32-byte aligned", op,
-                                             (unsigned long long)region_bases[m]);
-    if (region_bases[m] < header_bytes)
-      return set_err(KVS_E_INVAL, "%s: member %u's region at %llu B overlaps the %u B header", op, m,
-                     (unsigned long long)region_bases[m], header_bytes);
-    const uint64_t source_end = ((uint64_t)max_block + 1) * sbb;
-    if (source_end > member_extent[m])
-      return set_err(KVS_E_INVAL, "%s: block %u reaches past member %u's %llu B shard", op, max_block, m,
-                     (unsigned long long)member_extent[m]);
-    const uint64_t end = region_bases[m] + (uint64_t)n_blocks * sbb * n_ranks;
-    if (end > blob_bytes)
-      return set_err(KVS_E_INVAL, "%s: member %u's region ends at %llu B, past the %llu B blob", op, m,
-                     (unsigned long long)end, (unsigned long long)blob_bytes);
-    for (uint32_t r = 0; r < n_ranks; ++r)
-      if (!member_ptrs[(uint64_t)r * n_members + m])
-        return set_err(KVS_E_INVAL, "%s: member %u of rank %u is null", op, m, r);
-    tile_prefix[m + 1] = tile_prefix[m] + (sbb + kTileBytes - 1) / kTileBytes;
-  }
-  cudaPointerAttributes a{};
-  if (cudaPointerGetAttributes(&a, blob) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
-    cudaGetLastError();
-    return set_err(KVS_E_INVAL, "%s: blob must be device memory", op);
-  }
-  DeviceGuard g(a.device);
-  // members on other GPUs are read / written over NVLink: enable peer access to their devices
-  for (uint64_t i = 0; i < (uint64_t)n_ranks * n_members; ++i) {
-    cudaPointerAttributes ma{};
-    if (cudaPointerGetAttributes(&ma, reinterpret_cast<const void *>(member_ptrs[i])) != cudaSuccess ||
-        ma.type != cudaMemoryTypeDevice) {
-      cudaGetLastError();
-      return set_err(KVS_E_INVAL, "%s: member tensor must be device memory", op);
-    }
-    if (ma.type == cudaMemoryTypeDevice && ma.device != a.device) {
-      cudaError_t pe = cudaDeviceEnablePeerAccess(ma.device, 0);
-      if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
-      else if (pe != cudaSuccess) return set_err(KVS_E_CUDA, "%s: enable peer access %d->%d: %s", op, a.device,
-                                                 ma.device, cudaGetErrorString(pe));
-    }
-  }
-  // per-call device metadata: allocated from a small stream-ordered pool (cudaMallocAsync)
-  const uint64_t nrm = (uint64_t)n_ranks * n_members;
-  const size_t bytes = 8 * (nrm + 3ull * n_members + 1 + n_blocks + 1) + 4ull * n_header_words + 64;
-  std::vector<uint8_t> hostbuf(bytes, 0);
-  size_t off = 0;
-  auto put = [&](const void *src, size_t n) {
-    off = (off + 15) & ~size_t(15);
-    const size_t o = off;
-    if (n) std::memcpy(hostbuf.data() + o, src, n);
-    off += n;
-    return o;
-  };
-  hostbuf.resize(bytes + 16 * 8);
-  std::vector<int64_t> ids64(block_ids, block_ids + n_blocks);
-  const uint64_t blob_addr = reinterpret_cast<uint64_t>(blob);
-  const size_t o_mp = put(member_ptrs, 8 * nrm);
-  const size_t o_mb = put(member_block_bytes, 8ull * n_members);
-  const size_t o_rb = put(region_bases, 8ull * n_members);
-  const size_t o_tp = put(tile_prefix.data(), 8ull * (n_members + 1));
-  const size_t o_id = put(ids64.data(), 8ull * n_blocks);
-  const size_t o_bl = put(&blob_addr, 8);
-  const size_t o_hw = put(header_words, 4ull * n_header_words);
+  const kvs::ChunkArgs a{member_ptrs, n_ranks,      n_members,      member_block_bytes, member_extent, block_ids,
+                         n_blocks,    region_bases, header_words,   n_header_words,     blob,          blob_bytes,
+                         to_blob};
+  kvs::ChunkMeta m{};
+  TRY(kvs::check_chunk_args(a, op, &m));
+  DeviceGuard g(m.device);
+  // per-call device metadata: allocated from the stream-ordered pool (cudaMallocAsync)
+  std::vector<uint8_t> image(m.bytes);
+  kvs::pack_chunk_meta(a, m, image.data());
   cudaStream_t s = (cudaStream_t)stream;
   uint8_t *dbuf = nullptr;
-  CUDA_TRY(cudaMallocAsync(&dbuf, off, s));
-  CUDA_TRY(cudaMemcpyAsync(dbuf, hostbuf.data(), off, cudaMemcpyHostToDevice, s));
-  kvs::ChunkCopyParams p{};
-  p.member_ptrs = reinterpret_cast<const uint64_t *>(dbuf + o_mp);
-  p.member_bytes = reinterpret_cast<const uint64_t *>(dbuf + o_mb);
-  p.region_bases = reinterpret_cast<const uint64_t *>(dbuf + o_rb);
-  p.tile_prefix = reinterpret_cast<const uint64_t *>(dbuf + o_tp);
-  p.block_ids = reinterpret_cast<const int64_t *>(dbuf + o_id);
-  p.blob_ptrs = reinterpret_cast<const uint64_t *>(dbuf + o_bl);
-  p.header_words = reinterpret_cast<const uint32_t *>(dbuf + o_hw);
-  p.n_header_words = to_blob ? n_header_words : 0;
-  p.n_blobs = 1;
-  p.blocks_per_blob = n_blocks;
-  p.n_ranks = n_ranks;
-  p.n_members = n_members;
-  p.tile_bytes = kTileBytes;
-  p.tiles_per_combo = tile_prefix[n_members];
-  p.total_tiles = (uint64_t)n_blocks * n_ranks * p.tiles_per_combo;
-  p.to_blob = to_blob;
-  CUDA_TRY(launch_copy(p, s, true, nullptr));
+  CUDA_TRY(cudaMallocAsync(&dbuf, m.bytes, s));
+  CUDA_TRY(cudaMemcpyAsync(dbuf, image.data(), m.bytes, cudaMemcpyHostToDevice, s));
+  CUDA_TRY(kvs::launch_chunk(kvs::chunk_params(a, m, dbuf), s));
   CUDA_TRY(cudaFreeAsync(dbuf, s));
-  // the host buffer was consumed by a pageable copy, which completes before returning
+  // the host image was consumed by a pageable copy, which returns once the image is staged
   return KVS_OK;
 }
 

@@ -185,6 +185,17 @@ class Server:
         )
         return host, dev
 
+    def set_write_through_timing(self, enable: bool) -> None:
+        """Bracket every batch of write-through copies with CUDA events on the write-through stream."""
+        check(load().kvs_server_set_timing(self._handle(), 1 if enable else 0))
+
+    def write_through_timing(self) -> dict[str, float]:
+        """Totals since the last call: batches ("launches"), bytes copied to the host tier and their
+        device time (total_ms)."""
+        t = _native.KernelTiming()
+        check(load().kvs_server_write_through_timing(self._handle(), C.byref(t)))
+        return struct_to_dict(t)
+
     def _test_put_drain_progress(self) -> tuple[int, int]:
         i, c = C.c_uint32(), C.c_uint32()
         check(load().kvs_server_put_drain_progress(self._handle(), C.byref(i), C.byref(c)))
@@ -483,6 +494,13 @@ class Client:
         g, s = _native.KernelTiming(), _native.KernelTiming()
         check(load().kvs_client_timing(self._handle(), C.byref(g), C.byref(s)))
         return {"gather": struct_to_dict(g), "scatter": struct_to_dict(s)}
+
+    def host_tier_timing(self) -> dict[str, dict[str, float]]:
+        """Totals since the last call of the host-tier copy launches of gets (timing on):
+        {"admissions": {...}, "serves": {...}} (launches, bytes, total_ms)."""
+        a, s = _native.KernelTiming(), _native.KernelTiming()
+        check(load().kvs_client_host_tier_timing(self._handle(), C.byref(a), C.byref(s)))
+        return {"admissions": struct_to_dict(a), "serves": struct_to_dict(s)}
 
     def __enter__(self) -> "Client":
         return self

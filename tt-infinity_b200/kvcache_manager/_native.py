@@ -213,6 +213,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kvs_client_set_timing": (C.c_int, [P, C.c_int]),
     "kvs_client_timing": (C.c_int, [P, C.POINTER(KernelTiming), C.POINTER(KernelTiming)]),
+    "kvs_client_host_tier_timing": (C.c_int, [P, C.POINTER(KernelTiming), C.POINTER(KernelTiming)]),
+    "kvs_server_set_timing": (C.c_int, [P, C.c_int]),
+    "kvs_server_write_through_timing": (C.c_int, [P, C.POINTER(KernelTiming)]),
     "kvs_gather_chunk": (
         C.c_int,
         [_u64p, C.c_uint32, C.c_uint32, _u64p, _u64p, _u32p, C.c_uint32, _u64p, _u32p, C.c_uint32, P, C.c_uint64, P],
@@ -225,6 +228,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         C.c_int,
         [P, C.c_uint64, _u64p, C.c_uint32, C.c_uint32, _u64p, _u64p, _u32p, C.c_uint32, _u64p, P],
     ),
+    "kvs_copy_engine_status": (C.c_int, [C.c_int32, _u32p, _u32p]),
+    "kvs_set_copy_wait_limit": (C.c_int, [C.c_int64]),
 }
 
 _lib = None
