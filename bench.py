@@ -64,6 +64,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-multiturn", action="store_true",
+                    help="N=1: skip the config-3 multi-turn host-tier run that follows the main step")
     ap.add_argument("--latency-samples", type=int, default=200)
     ap.add_argument("--sweep", action="store_true",
                     help="fp8 + per-block-scale layout, batches of 1..4096 blocks (prints a sweep table)")
@@ -193,6 +195,73 @@ def build_pool(torch, device, rank=0):
     return kv
 
 
+def _bits(t):
+    """The tensor's bytes as integers (float compares would treat -0 / +0 as equal and NaN as unequal)."""
+    import torch
+
+    return t.contiguous().view(torch.uint8)
+
+
+def byte_gate(torch, members, src, dst, device, snapshot=None):
+    """Bit-exact check that block dst[i] of every member holds what block src[i] held (the current
+    source blocks, or `snapshot[m]` taken before the sources could change). Raises on a mismatch."""
+    di = torch.as_tensor(np.asarray(dst), device=device)
+    si = None if snapshot is not None else torch.as_tensor(np.asarray(src), device=device)
+    checked = 0
+    for m, t in enumerate(members):
+        want = snapshot[m] if snapshot is not None else t.index_select(0, si)
+        got = t.index_select(0, di)
+        if not torch.equal(_bits(got), _bits(want)):
+            raise RuntimeError(f"member {m}: restored blocks differ from the source blocks")
+        checked += got.numel() * got.element_size()
+    return {"check": "byte compare of every restored block with its source, every member tensor",
+            "members": len(members), "blocks": int(di.numel()), "bytes": int(checked)}
+
+
+def pcie_peaks(torch, device, stream, nbytes=1 << 30):
+    """(device->host, host->device) GB/s of a pinned 1 GiB copy, best of 3, CUDA events."""
+    pin = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    out = []
+    for to_host in (True, False):
+        best = 0.0
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if to_host:
+                pin.copy_(dev, non_blocking=True)
+            else:
+                dev.copy_(pin, non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            best = max(best, nbytes / (e0.elapsed_time(e1) / 1e3) / GB)
+        out.append(best)
+    del pin, dev
+    return out[0], out[1]
+
+
+def write_through_summary(wt, expected_bytes, d2h_peak):
+    """The write-through's own device time (CUDA events on the shard's write-through stream)."""
+    ms = wt["total_ms"]
+    achieved = wt["bytes"] / max(ms / 1e3, 1e-12) / GB
+    return {"bytes": int(wt["bytes"]), "expected_bytes": int(expected_bytes), "batches": int(wt["launches"]),
+            "device_ms": round(ms, 3), "achieved_GBps": round(achieved, 2), "pcie_d2h_peak_GBps": round(d2h_peak, 2),
+            "frac": round(achieved / d2h_peak, 4) if d2h_peak else None,
+            "how": "CUDA events on the write-through stream around each put's device->host copies",
+            "note": "every put is written through to the pinned host tier and the next get waits for it "
+                    "(the reference's commit barrier)"}
+
+
+def step_split(elapsed_ms, steps, gather, scatter, wt):
+    """Per step: the copy kernels' and the write-through's own device time, and the rest."""
+    kern = (gather["total_ms"] + scatter["total_ms"]) / steps
+    wt_ms = wt["total_ms"] / steps
+    step = elapsed_ms / steps
+    return {"step": round(step, 3), "copy_kernels": round(kern, 3), "write_through": round(wt_ms, 3),
+            "rest": round(step - kern - wt_ms, 3),
+            "note": "rest = lookups, replica updates, host catalog work and the ordering between them"}
+
+
 def run_ours(args, rank, local_rank, world):
     import torch
     import torch.distributed as dist
@@ -228,15 +297,11 @@ def run_ours(args, rank, local_rank, world):
             raise RuntimeError(f"step {step}: device-tier get missed {int((~found).sum())} blocks")
         return keys, src, dst
 
-    # correctness gate before timing: restored blocks equal the sources (checksums)
+    # correctness gate before timing: every restored block equals its source, byte for byte, in
+    # every one of the 128 member tensors (64 layers x K, V)
     keys, src, dst = one_step(0)
     torch.cuda.synchronize()
-    for layer in (0, LAYERS // 2, LAYERS - 1):
-        for t in kv[layer]:
-            a = t[torch.as_tensor(src, device=device)].view(torch.int16).to(torch.int64).sum()
-            b = t[torch.as_tensor(dst, device=device)].view(torch.int16).to(torch.int64).sum()
-            if int(a) != int(b):
-                raise RuntimeError("restored blocks differ from the source blocks")
+    gate = byte_gate(torch, [t for pair in kv for t in pair], src, dst, device)
     for w in range(args.warmup):
         one_step(1 + w)
     torch.cuda.synchronize()
@@ -249,6 +314,8 @@ def run_ours(args, rank, local_rank, world):
         sampler.start()
     client.kernel_timing()
     client.set_kernel_timing(True)
+    server.write_through_timing()
+    server.set_write_through_timing(True)
     launches0 = lib.kvs_kernel_launch_count()
     stream = torch.cuda.current_stream(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -265,6 +332,8 @@ def run_ours(args, rank, local_rank, world):
     elapsed_ms = start.elapsed_time(end)
     timing = client.kernel_timing()
     client.set_kernel_timing(False)
+    wt = server.write_through_timing()
+    server.set_write_through_timing(False)
     clocks = sampler.stop() if sampler else None
     if world > 1:
         t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
@@ -309,18 +378,9 @@ def run_ours(args, rank, local_rank, world):
     p50 = lat[len(lat) // 2]
     p99 = lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)]
 
-    # ---- PCIe device->host copy peak (pinned), the bound of the host write-through
-    pin = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
-    src_buf = torch.empty(1 << 30, dtype=torch.uint8, device=device)
-    best = 0.0
-    for _ in range(3):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        pin.copy_(src_buf, non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        best = max(best, (1 << 30) / (e0.elapsed_time(e1) / 1e3) / GB)
-    del pin, src_buf
+    # ---- PCIe copy peaks (pinned, 1 GiB, best of 3): device->host bounds the write-through,
+    # host->device the host-tier admissions
+    best, h2d_best = pcie_peaks(torch, device, stream)
 
     # ---- roofline of the dominant kernel (gather or scatter, by device time)
     peak, peak_kind = measured_peaks()
@@ -352,6 +412,7 @@ def run_ours(args, rank, local_rank, world):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) bf16 KV, random block tables, 64-bit chained prefix-hash keys",
+        "parity": gate,
         "config": {
             "workload": WORKLOAD,
             "layers": LAYERS, "kv_heads": HEADS, "head_dim": HEAD_DIM, "block_tokens": BLOCK_TOKENS,
@@ -381,13 +442,11 @@ def run_ours(args, rank, local_rank, world):
             "scatter_get": {"launches": s["launches"], "avg_ms": round(s["total_ms"] / max(1, s["launches"]), 4),
                             "GBps_2x_payload": round(2 * s["bytes"] / max(1e-9, s["total_ms"] / 1e3) / GB, 1)},
         },
-        "write_through": {
-            "bytes_per_step": BATCH_BLOCKS * BLOCK_PAYLOAD,
-            "achieved_GBps": round(BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB, 2),
-            "pcie_d2h_peak_GBps": round(best, 2),
-            "frac": round(BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB / best, 4),
-            "note": "every put is written through to the pinned host tier and get waits for it (commit barrier)",
-        },
+        "write_through": write_through_summary(wt, BATCH_BLOCKS * BLOCK_PAYLOAD * args.steps, best),
+        "step_split_ms": step_split(elapsed_ms, args.steps, g, s, wt),
+        "pcie_peaks_GBps": {"d2h": round(best, 2), "h2d": round(h2d_best, 2),
+                            "how": "torch copy of 1 GiB between device memory and pinned host memory, best of 3, "
+                                   "CUDA events"},
         "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
                                      "samples": len(lat),
                                      "note": "one committed device-resident block per Client.get_blocks call, "
@@ -402,7 +461,52 @@ def run_ours(args, rank, local_rank, world):
 
 # ------------------------------------------------------------------ hash-sharded store over N GPUs
 
-NVLINK_PEER_GBS = 770.0  # measured peer copy per direction on this pool's B200s (nominal 900)
+NVLINK_NOMINAL_GBS = 900.0  # NVLink 5 per direction per GPU (nominal)
+
+
+def _peer_copy_rates(torch, dist, device, nbytes=1 << 30):
+    """Measured NVLink rate per direction: every rank copies 1 GiB from its GPU into the next rank's
+    GPU with cudaMemcpyAsync (the copy engines, not this library's kernels), all ranks at once,
+    best of 3, CUDA events. Returns (this rank's GB/s, min over ranks)."""
+    import ctypes as C
+
+    from cuda.bindings import runtime as cudart
+
+    from kvcache_manager import _native
+
+    lib = _native.load()
+    rank, world = dist.get_rank(), dist.get_world_size()
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    src = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    h, off = _native.IpcHandle(), C.c_uint64()
+    _native.check(lib.kvs_ipc_export(C.c_void_p(buf.data_ptr()), C.byref(h), C.byref(off)))
+    handles = [None] * world
+    dist.all_gather_object(handles, (bytes(h.bytes), off.value))
+    peer = (rank + 1) % world
+    ph = _native.IpcHandle()
+    C.memmove(ph.bytes, handles[peer][0], 64)
+    base = C.c_void_p()
+    _native.check(lib.kvs_ipc_open(device, C.byref(ph), C.byref(base)))
+    dst = base.value + handles[peer][1]
+    stream = torch.cuda.current_stream(device)
+    best = 0.0
+    for _ in range(3):
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        err, = cudart.cudaMemcpyAsync(dst, src.data_ptr(), nbytes, cudart.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                      stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if err != cudart.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"peer copy: {err}")
+        best = max(best, nbytes / (e0.elapsed_time(e1) / 1e3) / GB)
+    dist.barrier()  # every copy into a peer's buffer has finished before any buffer goes away
+    lib.kvs_ipc_close(device, base)
+    dist.barrier()
+    del buf, src
+    return best, -_max_over_ranks(torch, dist, -best, device)
 
 
 def _max_over_ranks(torch, dist, value, device):
@@ -519,19 +623,24 @@ def run_sharded(args, rank, local_rank, world):
         prev["keys"], prev["src"] = keys, src
         return gd
 
-    def checksums(blocks):
-        idx = torch.as_tensor(blocks, device=device)
-        return [int(t[idx].view(torch.int16).to(torch.int64).sum()) for layer in (0, LAYERS // 2, LAYERS - 1)
-                for t in kv[layer]]
-
-    # correctness gate: blocks restored from the (mostly remote) shards equal their sources
+    # correctness gate: the blocks restored from the (mostly remote) shards equal their sources
+    # byte for byte in every member tensor; the sources are snapshotted first (2 GiB), since the
+    # next step's gets may land in them
+    members = [t for pair in kv for t in pair]
     one_step(0)
     torch.cuda.synchronize()
-    want = checksums(prev["src"])
+    src_idx = torch.as_tensor(prev["src"], device=device)
+    snap = [t.index_select(0, src_idx) for t in members]
     got_blocks = one_step(1)
     torch.cuda.synchronize()
-    if checksums(got_blocks) != want:
-        raise RuntimeError(f"rank {rank}: restored blocks differ from the source blocks")
+    try:
+        gate, bad = byte_gate(torch, members, None, got_blocks, device, snapshot=snap), 0.0
+    except RuntimeError as exc:
+        gate, bad = str(exc), 1.0
+    del snap, src_idx
+    if _max_over_ranks(torch, dist, bad, device) > 0:  # every rank stops together
+        raise RuntimeError(f"rank {rank}: restored blocks differ from their sources somewhere: {gate}")
+    gate["ranks"] = world
     for w in range(args.warmup):
         one_step(2 + w)
     torch.cuda.synchronize()
@@ -542,6 +651,8 @@ def run_sharded(args, rank, local_rank, world):
         sampler.start()
     eng.client.kernel_timing()
     eng.client.set_kernel_timing(True)
+    eng.server.write_through_timing()
+    eng.server.set_write_through_timing(True)
     c0 = dict(store.counters)
     launches0 = lib.kvs_kernel_launch_count()
     stream = torch.cuda.current_stream(device)
@@ -558,9 +669,16 @@ def run_sharded(args, rank, local_rank, world):
     elapsed_ms = _max_over_ranks(torch, dist, start.elapsed_time(end), device)
     timing = eng.client.kernel_timing()
     eng.client.set_kernel_timing(False)
+    wt = eng.server.write_through_timing()
+    eng.server.set_write_through_timing(False)
     c1 = dict(store.counters)
     clocks = sampler.stop() if sampler else None
     step_bytes = 2 * BATCH_BLOCKS * BLOCK_PAYLOAD
+    # this shard's write-through: its own device time; the slowest shard's bounds the step
+    wt_ms_step = wt["total_ms"] / args.steps
+    wt_gbps = wt["bytes"] / max(wt["total_ms"] / 1e3, 1e-12) / GB
+    wt_ms_max = _max_over_ranks(torch, dist, wt_ms_step, device)
+    wt_gbps_min = -_max_over_ranks(torch, dist, -wt_gbps, device)
     value = world * args.steps * step_bytes / (elapsed_ms / 1e3) / GB
     dom, kernels, nvlink_achieved = _nvlink_roofline(torch, dist, device, timing, c0, c1, BLOCK_PAYLOAD)
 
@@ -597,6 +715,7 @@ def run_sharded(args, rank, local_rank, world):
     rounds = (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps
     store.close()
     hw_mine, hw_min, hw_sum = _host_write_rates(torch, dist, device)
+    peer_mine, peer_min = _peer_copy_rates(torch, dist, device)
     wt_per_gpu = BATCH_BLOCKS * BLOCK_PAYLOAD / (elapsed_ms / args.steps / 1e3) / GB
     if rank != 0:
         return None
@@ -624,16 +743,32 @@ def run_sharded(args, rank, local_rank, world):
                 "h2d_bytes_per_step": 2 * 8 * world * sharded.request_words(BATCH_BLOCKS),
                 "d2h_bytes_per_step": 2 * 8 * world * sharded.reply_words(BATCH_BLOCKS)},
         "gpu_launches": int(launches),
+        "parity": gate,
         "roofline": {
-            "kernel": dom, "bound": "nvlink", "achieved": round(nvlink_achieved, 1), "peak": NVLINK_PEER_GBS,
-            "unit": "GB/s", "frac": round(nvlink_achieved / NVLINK_PEER_GBS, 4),
-            "peak_kind": "measured peer copy per direction (pool figure)", "traffic": None,
+            "kernel": dom, "bound": "nvlink", "achieved": round(nvlink_achieved, 1), "peak": NVLINK_NOMINAL_GBS,
+            "unit": "GB/s", "frac": round(nvlink_achieved / NVLINK_NOMINAL_GBS, 4),
+            "peak_kind": "nominal NVLink 5 per direction per GPU",
+            "measured_peer_copy_GBps": {"rank0": round(peer_mine, 1), "min": round(peer_min, 1),
+                                        "how": "cudaMemcpyAsync of 1 GiB into the next rank's GPU, all ranks at "
+                                               "once, best of 3, in this run"},
+            "frac_of_measured_peer_copy": round(nvlink_achieved / peer_min, 4) if peer_min else None,
+            "traffic": None,
             "algorithmic_bytes_per_launch": k["nvlink_bytes_per_launch"], "avg_launch_ms": k["avg_ms"],
             "hbm_peak": hbm_peak, "hbm_peak_kind": peak_kind,
         },
         "kernels": kernels,
+        "limiter": {
+            "step_ms": round(elapsed_ms / args.steps, 3),
+            "write_through_ms_slowest_shard": round(wt_ms_max, 3),
+            "push_kernels_ms_rank0": round((timing["gather"]["total_ms"] + timing["scatter"]["total_ms"]) / args.steps, 3),
+            "bound": ("host write-through (the next step's gets wait for it)" if wt_ms_max > 0.5 * elapsed_ms / args.steps
+                      else "NVLink pushes and the per-step protocol"),
+        },
         "write_through": {
             "bytes_per_step_per_gpu": BATCH_BLOCKS * BLOCK_PAYLOAD,
+            "device_ms_per_step_slowest_shard": round(wt_ms_max, 3),
+            "measured_GBps_rank0": round(wt_gbps, 2), "measured_GBps_min": round(wt_gbps_min, 2),
+            "how": "CUDA events on each shard's write-through stream around its device->host copies",
             "achieved_GBps_per_gpu": round(wt_per_gpu, 2),
             "concurrent_d2h_GBps_per_gpu": {"rank0": round(hw_mine, 2), "min": round(hw_min, 2)},
             "concurrent_d2h_GBps_all_gpus": round(hw_sum, 1),
@@ -750,7 +885,7 @@ def run_mix(args, rank, local_rank, world):
                  "grant_rounds_per_step": (c1["grant_rounds"] - c0["grant_rounds"]) / args.steps}
         if transport == "p2p":
             entry.update(roofline_kernel=dom, nvlink_achieved_GBps=round(nvl, 1),
-                         nvlink_frac=round(nvl / NVLINK_PEER_GBS, 4))
+                         nvlink_frac_of_nominal=round(nvl / NVLINK_NOMINAL_GBS, 4))
         else:
             # the copy kernels pack and unpack rows in this GPU's memory; NCCL moves them over NVLink
             for k in entry["kernels"].values():
@@ -869,7 +1004,7 @@ def run_reference(args, rank, world):
 # ------------------------------------------------------------------ fp8 batch sweep (latency vs bandwidth)
 
 FP8_LAYERS, FP8_HEADS, FP8_DIM, FP8_BLOCK_TOKENS = 80, 8, 128, 16
-FP8_POOL_BLOCKS = 32768  # 65,536 blocks (160 GiB) do not fit next to a slab; half the pool is used
+FP8_POOL_BLOCKS = 65536  # 160 GiB of fp8 blocks; the slab beside it holds the largest batch (4096 values)
 
 
 def fp8_layout(torch, device, pool_blocks):
@@ -900,11 +1035,12 @@ def run_sweep(args):
     payload = sum(layout.member_block_bytes)
     units = -(-vlen // UNIT_BYTES)
     block_units = 1 << (units - 1).bit_length()
-    server = Server(0, max_keys=2 * 4096 + 64, heap_bytes=(4096 + 64) * block_units * UNIT_BYTES,
-                    host_pool_bytes=(4096 + 64) * units * UNIT_BYTES)
+    server = Server(0, max_keys=2 * 4096 + 64, heap_bytes=(4096 + 4) * block_units * UNIT_BYTES,
+                    host_pool_bytes=(4096 + 4) * units * UNIT_BYTES)
     client = Client(0, server)
     rng = np.random.default_rng(9)
     rows = []
+    checked = 0
     for batch in [1, 4, 16, 64, 256, 1024, 4096]:
         put_ms, get_ms = [], []
         reps = max(2, min(20, 2048 // batch))
@@ -924,6 +1060,8 @@ def run_sweep(args):
             torch.cuda.synchronize()
             t3 = time.perf_counter()
             assert found.all()
+            if r == 0:  # untimed: payload and scale bytes of every restored block equal their sources
+                checked += byte_gate(torch, layout.members, src, dst, 0)["bytes"]
             for k in keys:  # keep the catalog bounded
                 client.delete(int(k))
             if r:
@@ -938,6 +1076,8 @@ def run_sweep(args):
     server.close()
     return {"sweep": "fp8 e4m3 KV + fp32 per-block scales, 80 layers x 8 heads x 128 dim, 16-token blocks",
             "pool_blocks": FP8_POOL_BLOCKS, "bytes_per_block": payload, "value_bytes": vlen,
+            "parity": {"check": "byte compare of every restored block (payload and scales) with its source, first "
+                                "repetition of every batch size", "bytes": checked},
             "note": "put = landed (gather into the slab, write-through then flushed outside the put time); get = "
                     "device-tier hit; wall clock around the Python API call",
             "rows": rows}
@@ -1015,17 +1155,28 @@ def run_multiturn(args):
     slab = max(block_bytes, working_set * block_bytes // 4)  # 25 % of the working set
     server = Server(0, max_keys=2 * working_set, heap_bytes=slab, host_pool_bytes=(working_set + 64) * units * UNIT_BYTES)
     client = Client(0, server)
+    stream = torch.cuda.current_stream(0)
+    d2h_peak, h2d_peak = pcie_peaks(torch, 0, stream)
     torch.cuda.synchronize()
+    client.set_kernel_timing(True)
+    server.set_write_through_timing(True)
     phase = {}
     t0 = time.perf_counter()
     st = run_multiturn_workload(client, layout, plan, pool, phase_s=phase)
     client.flush()
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
+    kt, ht, wt = client.kernel_timing(), client.host_tier_timing(), server.write_through_timing()
     sst = server.stats()
     client.close()
     server.close()
     payload = sum(layout.member_block_bytes)
+
+    def rate(t, peak):
+        gbps = t["bytes"] / max(t["total_ms"] / 1e3, 1e-12) / GB
+        return {"launches": int(t["launches"]), "bytes": int(t["bytes"]), "device_ms": round(t["total_ms"], 3),
+                "GBps": round(gbps, 2), "frac_of_peak": round(gbps / peak, 4) if peak else None}
+
     return {"multiturn": "32 sessions x 5 turns, U(512, 4096) tokens per turn, config-1 KV shape, slab = 25% of the working set",
             "working_set_blocks": working_set, "slab_bytes": slab, "wall_s": round(dt, 3),
             "blocks_restored": st["gets"], "blocks_put": st["puts"],
@@ -1034,6 +1185,16 @@ def run_multiturn(args):
             "victims_evicted": sst["victims_evicted"],
             "moved_GBps": round((st["gets"] + st["puts"]) * payload / dt / GB, 3),
             "host_s_by_call": {k: round(v, 4) for k, v in phase.items()},
+            "pcie_peaks_GBps": {"d2h": round(d2h_peak, 2), "h2d": round(h2d_peak, 2)},
+            "device_timed": {
+                "admissions_h2d": rate(ht["admissions"], h2d_peak),
+                "host_tier_hit_scatters": rate(ht["serves"], 0),
+                "write_through_d2h": rate(wt, d2h_peak),
+                "device_hit_scatters": rate(kt["scatter"], 0),
+                "put_gathers": rate(kt["gather"], 0),
+                "how": "CUDA events around each copy launch on the client stream and around each write-through "
+                       "batch on the shard's write-through stream; host-tier hit scatters read the slab blocks "
+                       "their admissions just filled (device memory), or the pinned copy when no block was free"},
             "pcie_bytes": {"h2d_admissions": sst["admissions"] * vlen, "d2h_write_through": sst["writes_through"] * vlen}}
 
 
@@ -1178,6 +1339,11 @@ def main():
             line = run_sharded(args, rank, local_rank, world)
         else:
             line = run_ours(args, rank, local_rank, world)
+            if world == 1 and line is not None and not args.no_multiturn:
+                import torch
+
+                torch.cuda.empty_cache()
+                line["multiturn_config3"] = run_multiturn(args)  # the host-tier path, on the same box
         if world > 1:
             import torch.distributed as dist
 
