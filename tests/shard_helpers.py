@@ -1,8 +1,8 @@
-"""Host-side helpers of the hash-sharded store across ranks (one process per GPU).
+"""Test helpers for the hash-sharded store across ranks (one process per GPU).
 
-The store shards keys by fnv1a32(key) % n_shards, the same function the C ABI applies
-(kvs_client_shard_of); these helpers let the host group a batch by owning shard and reduce a
-per-rank timing to the job's time (the max over ranks)."""
+A plain-Python restatement of the store's key placement (fnv1a32(key) % n_shards, the function
+the C ABI applies in kvs_client_shard_of), used by the tests to check the product's vectorised
+placement and to group a batch by owning shard; and the max-over-ranks reduction of a time."""
 
 from __future__ import annotations
 

@@ -10,7 +10,9 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from kvcache_manager import codec, dist as kdist
+from kvcache_manager import codec
+
+import shard_helpers as kdist
 
 
 def _free_port():

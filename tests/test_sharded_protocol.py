@@ -133,7 +133,7 @@ def test_pack_unpack_requests_round_trip():
 
 
 def test_shard_of_u64_matches_the_c_abi_function():
-    from kvcache_manager import dist as kdist
+    import shard_helpers as kdist
 
     keys = np.random.default_rng(2).integers(0, 2**64 - 1, 300, dtype=np.uint64)
     for n in (1, 2, 3, 8):

@@ -7,7 +7,7 @@
 // can replay it into the shard's HBM index replica before the next kernel that reads it.
 //
 // Policies that must match the reference exactly, because they decide which values stay in
-// the device cache (each restated from the reference and listed in DESIGN.md):
+// the device cache (each restated from the reference):
 //   * FNV-1a-32 open addressing, next_pow2(2 * max_keys) buckets, linear probe, every candidate
 //     revalidated against the entry, backward-shift delete (patch 0003 lines 9912-10057);
 //   * buddy value heap in `unit_bytes` units with LIFO free lists per order and aligned
