@@ -63,6 +63,11 @@ __device__ __forceinline__ int64_t block_id(const ChunkCopyParams &p, uint64_t i
   return p.block_ids ? p.block_ids[i] : p.inline_ids[i];
 }
 
+// Base address of blob b: from blob_ptrs, or from the parameters themselves.
+__device__ __forceinline__ uint64_t blob_ptr(const ChunkCopyParams &p, uint32_t b) {
+  return p.blob_ptrs ? p.blob_ptrs[b] : p.inline_blobs[b];
+}
+
 // Index of (blob, rank, member) in member_ptrs: blobs of member set s use the s-th group of
 // n_ranks x n_members pointers (several requesters' paged pools in one launch).
 __device__ __forceinline__ uint64_t member_index(const ChunkCopyParams &p, uint32_t blob, uint32_t rank, uint32_t m) {
@@ -77,7 +82,7 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const __grid_c
     for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < nh;
          g += (uint64_t)gridDim.x * blockDim.x) {
       const uint32_t b = (uint32_t)(g / p.n_header_words), w = (uint32_t)(g % p.n_header_words);
-      const uint64_t base = p.blob_ptrs[b];
+      const uint64_t base = blob_ptr(p, b);
       if (base) reinterpret_cast<uint32_t *>(base)[w] = p.header_words[w];
     }
   }
@@ -97,7 +102,7 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const __grid_c
     const uint64_t bc = combo / p.n_ranks;
     const uint32_t cb = (uint32_t)(bc % p.blocks_per_blob);
     const uint32_t blob = (uint32_t)(bc / p.blocks_per_blob);
-    const uint64_t blob_base = p.blob_ptrs[blob];
+    const uint64_t blob_base = blob_ptr(p, blob);
     if (blob_base == 0) continue;
     const uint64_t sbb = p.member_bytes[m];
     const uint64_t seg_off = tile_in_seg * p.tile_bytes;
@@ -105,12 +110,12 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const __grid_c
     const int64_t block = block_id(p, (uint64_t)blob * p.blocks_per_blob + cb);
     uint8_t *member = reinterpret_cast<uint8_t *>(p.member_ptrs[member_index(p, blob, r, m)]) +
                       (uint64_t)block * sbb + seg_off;
-    uint8_t *blob_ptr = reinterpret_cast<uint8_t *>(blob_base) + p.region_bases[m] +
-                        (uint64_t)cb * sbb * p.n_ranks + (uint64_t)r * sbb + seg_off;
+    uint8_t *blob_at = reinterpret_cast<uint8_t *>(blob_base) + p.region_bases[m] +
+                       (uint64_t)cb * sbb * p.n_ranks + (uint64_t)r * sbb + seg_off;
     if (p.to_blob)
-      cta_copy(blob_ptr, member, len);
+      cta_copy(blob_at, member, len);
     else
-      cta_copy(member, blob_ptr, len);
+      cta_copy(member, blob_at, len);
   }
 }
 
@@ -188,7 +193,7 @@ struct TileCursor {
     const uint64_t bc = combo / p->n_ranks;
     cb = (uint32_t)(bc % p->blocks_per_blob);
     blob = (uint32_t)(bc / p->blocks_per_blob);
-    blob_base = blob < p->n_blobs ? p->blob_ptrs[blob] : 0;
+    blob_base = blob < p->n_blobs ? blob_ptr(*p, blob) : 0;
     block = blob < p->n_blobs ? block_id(*p, (uint64_t)blob * p->blocks_per_blob + cb) : 0;
   }
   __device__ void init(const ChunkCopyParams *pp, uint64_t begin, uint64_t stop) {
@@ -258,7 +263,7 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const __gri
       const uint64_t total = (uint64_t)p.n_blobs * p.n_header_words;
       for (uint64_t g = (uint64_t)blockIdx.x * nh + h; g < total; g += (uint64_t)gridDim.x * nh) {
         const uint32_t b = (uint32_t)(g / p.n_header_words), w = (uint32_t)(g % p.n_header_words);
-        const uint64_t base = p.blob_ptrs[b];
+        const uint64_t base = blob_ptr(p, b);
         if (base) reinterpret_cast<uint32_t *>(base)[w] = p.header_words[w];
       }
     }
@@ -662,9 +667,10 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
   }
 }
 
-// Block ids from the parameters cover at most kInlineKeys (blob, chunk block) pairs.
+// Block ids and blob addresses from the parameters cover at most kInlineKeys entries.
 static bool inline_ids_fit(const ChunkCopyParams &p) {
-  return p.block_ids || (uint64_t)p.n_blobs * p.blocks_per_blob <= kInlineKeys;
+  return (p.block_ids || (uint64_t)p.n_blobs * p.blocks_per_blob <= kInlineKeys) &&
+         (p.blob_ptrs || p.n_blobs <= kInlineKeys);
 }
 
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas) {

@@ -64,7 +64,7 @@ struct ChunkCopyParams {
   const uint64_t *region_bases;  // [n_members] member region offset inside a blob
   const uint64_t *tile_prefix;   // [n_members + 1] tiles per member, prefix summed
   const int64_t *block_ids;      // [n_blobs * blocks_per_blob]; nullptr: inline_ids
-  const uint64_t *blob_ptrs;     // [n_blobs] blob base addresses; 0 skips the blob
+  const uint64_t *blob_ptrs;     // [n_blobs] blob base addresses; 0 skips the blob; nullptr: inline_blobs
   const uint32_t *header_words;  // [n_header_words] (gather only)
   uint32_t n_header_words;
   uint32_t n_blobs;
@@ -78,6 +78,7 @@ struct ChunkCopyParams {
   unsigned int *timeout_flag;  // optional host-mapped word set to 1 if a bounded wait expires
   uint32_t wait_polls;       // polls of one bounded wait on a tile load (set by the launcher)
   int64_t inline_ids[kInlineKeys];  // block ids when block_ids is nullptr (n_blobs * blocks_per_blob <= 8)
+  uint64_t inline_blobs[kInlineKeys];  // blob addresses when blob_ptrs is nullptr (n_blobs <= 8)
 };
 
 struct LookupParams {

@@ -1274,6 +1274,25 @@ int kvs_server_index_snapshot(kvs_server *s, uint32_t *host_pairs, uint32_t *dev
   if (cap_pairs < nb) return KVS_OK;
   DeviceGuard g(s->cfg.device);
   if (s->tail) CUDA_TRY(cudaEventSynchronize(s->tail));
+  // replica updates that no device lookup has needed yet (small gets answer on the host) are
+  // written now, so the snapshot shows the replica as the next probe will see it
+  for (uint32_t b : s->dir->take_dirty_buckets()) {
+    const uint64_t w = s->dir->bucket_word(b);
+    CUDA_TRY(cudaMemcpy(s->d_buckets + b, &w, 8, cudaMemcpyHostToDevice));
+  }
+  for (uint32_t slot : s->dir->take_dirty_slots()) {
+    const kvs::Entry &e = s->dir->entry(slot);
+    kvs::DevMeta m{};
+    m.value_off = e.value_off;
+    m.total_len = (uint32_t)e.total_len;
+    m.valid = e.valid;
+    m.location = e.location;
+    m.key_len = e.key_len;
+    CUDA_TRY(cudaMemcpy(s->d_meta + slot, &m, sizeof m, cudaMemcpyHostToDevice));
+  }
+  for (uint32_t slot : s->dir->take_dirty_keys())
+    CUDA_TRY(cudaMemcpy(s->d_keyrows + (uint64_t)slot * kvs::kKeyRowWords, s->dir->entry(slot).key,
+                        kvs::kMaxKeyBytes, cudaMemcpyHostToDevice));
   if (host_pairs) std::memcpy(host_pairs, s->dir->bucket_pairs(), 8ull * nb);
   if (device_pairs) {
     std::vector<uint64_t> w(nb);
@@ -1803,6 +1822,73 @@ struct GetTarget {
   const uint32_t *sets;          // [n] member set of each key, or nullptr (set 0)
 };
 
+// Gets of at most kInlineKeys keys on one shard whose hits are all device-resident: the host
+// catalog, which every get consults anyway, answers the few lookups in well under a microsecond,
+// so the scatter launches at once with the block ids and slab addresses in its parameters -- no
+// probe kernel, replica update or host-to-device copy goes before it, and the device replica's
+// pending updates wait for the next probe. A host-tier hit or a length mismatch leaves *served = 0
+// and the catalog untouched, and the general path runs. Runs after the commit barrier, with the
+// shard locked and the layout's arrays on the device (c->layout_dev).
+static int small_device_get(kvs_client *c, const GetTarget &t, uint32_t n, const uint64_t *keys,
+                            const int64_t *block_ids, uint32_t shard, uint8_t *found, void *stream, int *served) {
+  *served = 0;
+  kvs_server *s = c->shards[shard];
+  const BlockFormat &fmt = *t.fmt;
+  uint32_t slots[kvs::kInlineKeys];
+  for (uint32_t i = 0; i < n; ++i) {
+    slots[i] = s->dir->lookup((const uint8_t *)&keys[i], 8);
+    if (slots[i] == kvs::kBucketEmpty) continue;
+    const kvs::Entry &e = s->dir->entry(slots[i]);
+    if (e.total_len != fmt.value_len || e.location == kvs::kLocHost) return KVS_OK;
+  }
+  *served = 1;
+  kvs::ChunkCopyParams p{};
+  uint64_t payload_per_block = 0, hits = 0;
+  for (uint32_t m = 0; m < t.n_members; ++m) payload_per_block += t.member_bytes[m];
+  s->dir->take_evicted();
+  for (uint32_t i = 0; i < n; ++i) {
+    found[i] = 0;
+    p.inline_ids[i] = block_ids[i];
+    p.inline_blobs[i] = 0;  // a miss copies nothing
+    if (slots[i] == kvs::kBucketEmpty) continue;
+    uint64_t off = 0;
+    // recency in batch order, as the general path applies it: a device-resident hit moves to MRU
+    if (s->dir->get_hit(slots[i], &off) != Directory::GetAction::kDevice || !s->dir->take_evicted().empty())
+      return set_err(KVS_E_CUDA, "get_blocks: catalog placed device-resident key %u off the device", i);
+    p.inline_blobs[i] = s->slab_base() + s->dir->entry(slots[i]).value_off;
+    found[i] = 1;
+    ++hits;
+  }
+  if (!hits) return KVS_OK;  // every key missed: nothing to copy, no device work to order
+  TRY(begin_op(c, stream));
+  TRY(chain_wait(c, s));
+  const size_t lay_mb = 8ull * t.n_members, lay_rb = lay_mb + 8ull * t.n_members, lay_tp = lay_rb + 8ull * t.n_members;
+  p.member_ptrs = reinterpret_cast<const uint64_t *>(c->layout_dev);
+  p.member_bytes = reinterpret_cast<const uint64_t *>(c->layout_dev + lay_mb);
+  p.region_bases = reinterpret_cast<const uint64_t *>(c->layout_dev + lay_rb);
+  p.tile_prefix = reinterpret_cast<const uint64_t *>(c->layout_dev + lay_tp);
+  p.block_ids = nullptr;
+  p.blob_ptrs = nullptr;
+  p.n_blobs = n;
+  p.blocks_per_blob = 1;
+  p.n_ranks = 1;
+  p.n_members = t.n_members;
+  p.tile_bytes = kTileBytes;
+  p.tiles_per_combo = fmt.tile_prefix.back();
+  p.total_tiles = (uint64_t)n * p.tiles_per_combo;
+  p.to_blob = 0;
+  cudaEvent_t t0 = nullptr;
+  c->time_begin(&t0);
+  CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
+  c->time_end(t0, 1, hits * payload_per_block);
+  s->launches++;
+  TRY(chain_record(c, shard));
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  TRY(check_tma_timeouts(c, "get_blocks"));
+  // no end_op: the client stream is idle after the synchronise
+  return KVS_OK;
+}
+
 static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const uint64_t *keys,
                            const int64_t *block_ids, uint8_t *found, void *stream) {
   const BlockFormat &fmt = *t.fmt;
@@ -1816,14 +1902,7 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
   const ShardOrder ord = order_by_shard(si, ns);
   ShardLocks locks(involved_servers(c, inv));
   TRY(quarantine_on_error(c, commit_barrier(c, inv)));  // GET preserves host-commit ordering first
-  TRY(begin_op(c, stream));
   const uint64_t ptr_bytes = 8ull * t.n_sets * t.n_members;
-  // ---- pass 1: replica update, device lookup, scatter of device hits
-  Staging &st = c->stage;
-  size_t need = 4096 + 68ull * n + ptr_bytes + 32ull * t.n_members;
-  for (size_t i = 0; i < ns; ++i)
-    if (inv[i]) need += mutation_upper_bound(c->shards[i]);
-  TRY(st.begin(need, c->stream));
   // the layout arrays, back to back as the device copy holds them
   const size_t lay_mb = ptr_bytes, lay_rb = lay_mb + 8ull * t.n_members, lay_tp = lay_rb + 8ull * t.n_members;
   const size_t lay_bytes = lay_tp + 8ull * (t.n_members + 1);
@@ -1833,10 +1912,23 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
   std::memcpy(lay.data() + lay_mb, t.member_bytes, 8ull * t.n_members);
   std::memcpy(lay.data() + lay_rb, fmt.region_bases.data(), 8ull * t.n_members);
   std::memcpy(lay.data() + lay_tp, fmt.tile_prefix.data(), 8ull * (t.n_members + 1));
-  // A small get on one shard with no index updates to apply and a layout already on the device
-  // needs no host-to-device copy: its keys and block ids travel in the kernel parameters.
+  // A small get on one shard with a layout already on the device needs no host-to-device copy:
+  // its keys and block ids travel in the kernel parameters.
   const bool layout_cached = !t.sets && c->layout_key.size() == lay_bytes &&
                              std::memcmp(c->layout_key.data(), lay.data(), lay_bytes) == 0;
+  if (layout_cached && n <= kvs::kInlineKeys && ord.run_shard.size() == 1) {
+    int served = 0;
+    const int rc = small_device_get(c, t, n, keys, block_ids, ord.run_shard[0], found, stream, &served);
+    if (served || rc != KVS_OK) return rc;
+  }
+  TRY(begin_op(c, stream));
+  // ---- pass 1: replica update, device lookup, scatter of device hits
+  Staging &st = c->stage;
+  size_t need = 4096 + 68ull * n + ptr_bytes + 32ull * t.n_members;
+  for (size_t i = 0; i < ns; ++i)
+    if (inv[i]) need += mutation_upper_bound(c->shards[i]);
+  TRY(st.begin(need, c->stream));
+  // with no index updates to apply either, the probe's keys travel in its parameters too
   bool inline_call = layout_cached && n <= kvs::kInlineKeys && ord.run_shard.size() == 1;
   if (inline_call) {
     size_t nb, nm, nk;
