@@ -65,7 +65,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-multiturn", action="store_true",
-                    help="N=1: skip the config-3 multi-turn host-tier run that follows the main step")
+                    help="N=1: skip the config-3 multi-turn and connector-restore runs that follow the main step")
     ap.add_argument("--latency-samples", type=int, default=200)
     ap.add_argument("--sweep", action="store_true",
                     help="fp8 + per-block-scale layout, batches of 1..4096 blocks (prints a sweep table)")
@@ -82,6 +82,8 @@ def parse() -> argparse.Namespace:
                     help="sharded store: P2P stores over NVLink (default) or NCCL send/recv of packed values")
     ap.add_argument("--mix", action="store_true",
                     help="hash-sharded 70/30 get/put mix of 256-block batches, config-1 KV shape, both transports")
+    ap.add_argument("--restore", action="store_true",
+                    help="the connector's batched restore of a Qwen3-32B-shaped 8192-token prompt (64 layers)")
     ap.add_argument("--fill", action="store_true",
                     help="token-granular paged fill: 8192 tokens of 4 requests into 64 layers' caches")
     ap.add_argument("--resident", type=int, default=0,
@@ -1309,10 +1311,101 @@ def run_fill(args):
                                                    "frac": round(all_achieved / peak, 4), "unit": "GB/s"}}}
 
 
+def run_restore(args):
+    """The connector's batched restore of a Qwen3-32B-shaped prompt: vLLM-layout caches of 64 layers
+    ([2, 4096 blocks, 64 tokens, 8 KV heads, 128] bf16), an 8192-token request stored as 32 chunks of
+    256 tokens (the raw-byte chunk blobs, 64 MiB each), its blocks cleared, then restored by
+    GPUConnector.batched_to_gpu: one store call whose fill launch writes every chunk into all 64
+    layers from the slab. Kernel time from the client's CUDA events; algorithmic bytes = read +
+    write of every restored row (2 x payload); the whole call's wall time beside it."""
+    import asyncio
+
+    import torch
+
+    from kvcache_manager import Client, Server
+    from kvcache_manager.connector import GPUConnector, KVCacheClient, RemoteConnector, kv_caches_from_vllm, raw_codec_for
+
+    class _Key:
+        def __init__(self, s):
+            self.s = s
+
+        def to_string(self):
+            return self.s
+
+    torch.cuda.set_device(0)
+    layers, nb, bs, tokens, chunk = (8 if args.small else LAYERS), POOL_BLOCKS, BLOCK_TOKENS, 8192, 256
+    g = torch.Generator(device="cuda")
+    g.manual_seed(21)
+    vllm = [torch.empty((2, nb, bs, HEADS, HEAD_DIM), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
+            for _ in range(layers)]
+    caches = kv_caches_from_vllm(vllm)
+    raw = raw_codec_for(caches, bs)
+    rng = np.random.default_rng(21)
+    first = int(rng.integers(0, nb - tokens // bs))  # the request's blocks: one contiguous run
+    slots = torch.arange(first * bs, first * bs + tokens, device="cuda")
+    n_chunks = tokens // chunk
+    vlen = raw.device_shard_plan(caches, layers, slots[:chunk].tolist(), 0)["value_len"]
+    units = -(-vlen // UNIT_BYTES)
+    block_units = 1 << (units - 1).bit_length()
+    server = Server(0, max_keys=4 * n_chunks, heap_bytes=(n_chunks + 2) * block_units * UNIT_BYTES,
+                    host_pool_bytes=(n_chunks + 2) * units * UNIT_BYTES, max_value_bytes=vlen)
+    client = Client(0, server)
+    kc = KVCacheClient(client, raw)
+    gpu = GPUConnector(kc, num_layers=layers, block_size=bs)
+    remote = RemoteConnector(kc, allocate=lambda shape, dtype, fmt=None: object(), meta_shape=(1,), meta_dtype=None)
+    starts = [i * chunk for i in range(n_chunks)]
+    ends = [s0 + chunk for s0 in starts]
+    keys = [_Key(f"prompt@{i}") for i in range(n_chunks)]
+    mos = [object() for _ in keys]
+    gpu.batched_from_gpu(mos, starts, ends, kvcaches=vllm, slot_mapping=slots)
+    asyncio.run(remote.batched_put(keys, mos))
+    client.flush()
+    blocks = slice(first, first + tokens // bs)
+    want = [t[:, blocks].clone() for t in vllm]
+    times, walls = [], []
+    for it in range(args.warmup + args.steps):
+        for t in vllm:
+            t[:, blocks].zero_()
+        torch.cuda.synchronize()
+        phs = asyncio.run(remote.batched_get(keys))
+        client.kernel_timing()
+        client.set_kernel_timing(True)
+        t0 = time.perf_counter()
+        gpu.batched_to_gpu(phs, starts, ends, kvcaches=vllm, slot_mapping=slots)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        kt = client.kernel_timing()["scatter"]
+        client.set_kernel_timing(False)
+        if it == 0:  # untimed: every restored byte equals what was stored
+            for t, w in zip(vllm, want):
+                if not torch.equal(t[:, blocks].view(torch.int16), w.view(torch.int16)):
+                    raise RuntimeError("restored blocks differ from the stored chunks")
+        if it >= args.warmup:
+            times.append(kt["total_ms"])
+            walls.append(wall * 1e3)
+    client.close()
+    server.close()
+    payload = 2 * layers * tokens * HEADS * HEAD_DIM * 2
+    ms = statistics.mean(times)
+    achieved = 2 * payload / (ms / 1e3) / GB
+    peak, kind = measured_peaks()
+    wall_ms = statistics.median(walls)
+    return {"restore": f"connector batched_to_gpu of {tokens} tokens in {n_chunks} chunks of {chunk}, {layers} layers "
+                       f"of vLLM-layout bf16 caches (8 KV heads x 128, {bs}-token blocks): one store call, one fill "
+                       "launch from the slab",
+            "payload_bytes": payload, "steps": len(times), "fill_ms": round(ms, 4), "call_wall_ms_p50": round(wall_ms, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind,
+                         "frac": round(achieved / peak, 4), "unit": "GB/s",
+                         "algorithmic_bytes_per_launch": 2 * payload},
+            "call_GBps_payload": round(payload / (wall_ms / 1e3) / GB, 1),
+            "parity": "byte compare of every restored block with the stored chunks (first call)"}
+
+
 def main():
     args = parse()
-    if args.sweep or args.multiturn or args.fill:
-        print(json.dumps(run_sweep(args) if args.sweep else run_multiturn(args) if args.multiturn else run_fill(args)))
+    if args.sweep or args.multiturn or args.fill or args.restore:
+        run = run_sweep if args.sweep else run_multiturn if args.multiturn else run_fill if args.fill else run_restore
+        print(json.dumps(run(args)))
         return
     rank, local_rank, world = dist_env()
     if args.mix and world == 1:
@@ -1344,6 +1437,8 @@ def main():
 
                 torch.cuda.empty_cache()
                 line["multiturn_config3"] = run_multiturn(args)  # the host-tier path, on the same box
+                torch.cuda.empty_cache()
+                line["restore_connector"] = run_restore(args)  # the connector's batched restore
         if world > 1:
             import torch.distributed as dist
 

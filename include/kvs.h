@@ -200,6 +200,31 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n,
 /* EXISTS over a batch of 64-bit keys through the device index; no recency update. */
 int kvs_exists_batch(kvs_client *c, uint32_t n, const uint64_t *keys, uint8_t *found);
 
+/* ---- chunk restore straight into a paged cache ----
+ * The store side of the connector's batched restore. The reference fetches each chunk's K / V and
+ * then fills the cache one layer per call with moreh_paged_fill_cache_varlen
+ * (TTGPUConnector.batched_to_gpu and _paged_fill_layer_coalesced, patch 0005 lines 6780-6870 and
+ * 11563-11770); here one paged-fill launch per 64 layers reads every chunk's rows where its value
+ * lives (the slab, or the pinned host tier) and writes them token by token.
+ * Key i names a raw-byte chunk value (patch 0005 lines 12258-12310): header words
+ * [0x524B564E, n_layers, 2 alloc_i x n_layers] zero padded to 32 bytes, then per layer the K region
+ * and the V region of alloc_i = ceil(tokens[i] / block_size) x block_size x row_bytes bytes each,
+ * one row_bytes row per token (the chunk blob kvs_gather_chunk writes from caches whose block is
+ * [block_size][row_bytes], e.g. vLLM's [num_blocks, block_size, heads, head_dim]). Row j < tokens[i]
+ * of layer l goes to cache_ks[l] / cache_vs[l] ([num_blocks][block_size][row_bytes], 16-byte
+ * aligned, row_bytes a multiple of 16) at position p = start_positions[i] + j: block
+ * page_table[i * max_blocks_per_chunk + p / block_size], row p % block_size; entries <= 0 skip the
+ * token, as in kvs_paged_fill_varlen. found[i] per key; a miss writes nothing; a stored value of
+ * another length fails the call with KVS_E_FORMAT before any state changes. Each key is a get
+ * (commit barrier first, recency, read-through admission, in key order). keys, key_lens, tokens,
+ * page_table, start_positions and found are host arrays; the caches are device memory of the
+ * client's GPU. Returns once the rows have landed. No counterpart entry point in the reference. */
+int kvs_restore_chunks(kvs_client *c, uint32_t n, const void *const *keys, const uint32_t *key_lens,
+                       const uint32_t *tokens, uint32_t n_layers, void *const *cache_ks, void *const *cache_vs,
+                       uint32_t num_blocks, uint32_t block_size, uint32_t row_bytes, const int32_t *page_table,
+                       uint32_t max_blocks_per_chunk, const int32_t *start_positions, uint8_t *found,
+                       void *stream);
+
 /* ---- hash sharding across processes (one process per GPU) ----
  * The reference serves several server worker groups behind one Fabric endpoint
  * (src/native/ttnn/server_runtime/server.cpp:80-86), each an independent directory; here each

@@ -26,6 +26,7 @@ class FakeStoreClient(KVCacheClient):
         super().__init__(client=None, raw_codec=None)
         self.store = {}
         self.restored = []
+        self.restore_calls = []
 
     def exists(self, key):
         return self.raw_key(key) in self.store
@@ -42,6 +43,10 @@ class FakeStoreClient(KVCacheClient):
         if hit:
             self.restored.append((key, list(slot_mapping_slice)))
         return hit
+
+    def get_chunks_device(self, keys, kvcaches, num_layers, slot_mapping_slices):
+        self.restore_calls.append(list(keys))
+        return [self.get_chunk_device(k, kvcaches, num_layers, sl) for k, sl in zip(keys, slot_mapping_slices)]
 
 
 def make():
@@ -80,6 +85,8 @@ def test_batched_paths_and_a_put_without_a_recorded_chunk():
     phs = asyncio.run(remote.batched_get(keys))
     gpu.batched_to_gpu(phs, [0, 64, 128], [64, 128, 192], kvcaches=caches, slot_mapping=slots)
     assert [k for k, _ in client.restored] == ["c0", "c1", "c2"]
+    assert client.restore_calls == [["c0", "c1", "c2"]]  # one store call restores the whole batch
+    assert gpu.load_misses == 0
     assert remote.support_batched_put() and remote.support_batched_get()
 
 

@@ -505,18 +505,21 @@ __device__ __forceinline__ uint32_t fill_valid_total(const int32_t *cu, uint32_t
 }
 
 // Cache row (for head 0) of token t, or -1 to skip it; *oor marks an out-of-range skip.
-__device__ __forceinline__ long long fill_row_of(const PagedFillParams &p, uint32_t t, bool *oor) {
+__device__ __forceinline__ long long fill_row_of(const PagedFillParams &p, uint32_t t, bool *oor, uint32_t *req,
+                                                 uint32_t *local) {
   uint32_t lo = 0, hi = p.batch;  // request of token t
   while (lo < hi) {
     const uint32_t mid = (lo + hi + 1) >> 1;
     if ((uint32_t)__ldg(p.cu_seqlens + mid) <= t) lo = mid; else hi = mid - 1;
   }
   *oor = false;
+  *req = lo;
   if (lo >= p.batch) {
     *oor = true;
     return -1;
   }
-  const uint32_t pos = t - (uint32_t)__ldg(p.cu_seqlens + lo) + (uint32_t)__ldg(p.start_positions + lo);
+  *local = t - (uint32_t)__ldg(p.cu_seqlens + lo);
+  const uint32_t pos = *local + (uint32_t)__ldg(p.start_positions + lo);
   const uint32_t vb = pos / p.block_size;
   if (vb >= p.max_blocks) {
     *oor = true;
@@ -536,7 +539,8 @@ __device__ __forceinline__ long long fill_row_of(const PagedFillParams &p, uint3
 // lane whose entry is not -1, and a token's request is found by binary lifting over shuffles
 // (cu_seqlens is non-decreasing up to the -1 padding, which compares as the largest value).
 __device__ __forceinline__ long long fill_row_small(const PagedFillParams &p, uint32_t cu_l, uint32_t sp_l,
-                                                    uint32_t t, bool want, bool *oor) {
+                                                    uint32_t t, bool want, bool *oor, uint32_t *req,
+                                                    uint32_t *local) {
   uint32_t r = 0;
 #pragma unroll
   for (uint32_t step = 16; step >= 1; step >>= 1) {
@@ -547,11 +551,13 @@ __device__ __forceinline__ long long fill_row_small(const PagedFillParams &p, ui
   const uint32_t cu_r = __shfl_sync(0xFFFFFFFFu, cu_l, r);
   const uint32_t sp_r = __shfl_sync(0xFFFFFFFFu, sp_l, r);
   *oor = false;
+  *req = r;
   if (!want) return -1;
   if (r >= p.batch) {
     *oor = true;
     return -1;
   }
+  *local = t - cu_r;
   const uint32_t pos = t - cu_r + sp_r;
   const uint32_t vb = pos / p.block_size;
   if (vb >= p.max_blocks) {
@@ -578,6 +584,9 @@ __device__ __forceinline__ PagedFillParams fill_layer(const PagedFillParams &p0,
   return p;
 }
 
+// kReq: request r's rows come from its own value (p.req_src, one head of row_bytes per token)
+// instead of the packed fill tensors; see PagedFillParams.
+template <bool kReq>
 __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFillParams p0, const FillLayers L) {
   const PagedFillParams p = fill_layer(p0, L);
   const uint32_t t0 = blockIdx.x * kFillTokens;
@@ -618,9 +627,16 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
     };
     int4 v[kFillUnroll];
     bool oor = false;
-    const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor)
-                                   : (lane < nt ? fill_row_of(p, t0 + lane, &oor) : -1);
+    uint32_t my_req = 0, my_local = 0;
+    const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor, &my_req, &my_local)
+                                   : (lane < nt ? fill_row_of(p, t0 + lane, &oor, &my_req, &my_local) : -1);
     if (oor && threadIdx.x < 32 && blockIdx.y == 0 && blockIdx.z == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
+    // kReq: this lane's token row in its request's value, for K (V is req_alloc further on)
+    uint64_t my_src = 0, my_alloc = 0;
+    if (kReq && my_row >= 0) {
+      my_alloc = __ldg(p.req_alloc + my_req);
+      my_src = __ldg(p.req_src + my_req) + 2ull * (p.layer0 + blockIdx.z) * my_alloc + (uint64_t)my_local * rb;
+    }
     // warp-uniform trip count (every lane joins the shuffles): run while the warp's lane 0 is in range
     for (uint32_t base = threadIdx.x; base - lane < total; base += kFillThreads * kFillUnroll) {
       uint64_t dst[kFillUnroll];
@@ -630,8 +646,16 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
         const bool live = i < total;
         uint32_t tok = 0, h = 0, side = 0, in_side = 0;
         const int4 *src = live ? src_of(i, &tok, &h, &side, &in_side) : nullptr;
-        if (live) v[u] = ld_stream(src);  // in bounds whether or not the token is written
         const long long row = __shfl_sync(0xFFFFFFFFu, my_row, tok);
+        if (kReq) {
+          // the token's row in its value: only tokens that are written have one
+          const uint64_t sk = __shfl_sync(0xFFFFFFFFu, my_src, tok);
+          const uint64_t sa = __shfl_sync(0xFFFFFFFFu, my_alloc, tok);
+          src = reinterpret_cast<const int4 *>(sk + (side ? sa : 0) + (uint64_t)(in_side - tok * wpr) * 16u);
+          if (live && row >= 0) v[u] = ld_stream(src);
+        } else if (live) {
+          v[u] = ld_stream(src);  // in bounds whether or not the token is written
+        }
         dst[u] = 0;
         if (live && row >= 0) {
           uint8_t *cache = side ? p.cache_v : p.cache_k;
@@ -643,10 +667,11 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
       for (int u = 0; u < kFillUnroll; ++u)
         if (dst[u]) st_stream(reinterpret_cast<int4 *>(dst[u]), v[u]);
     }
-  } else {
+  } else if (!kReq) {
     bool oor = false;
-    const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor)
-                                   : (lane < nt ? fill_row_of(p, t0 + lane, &oor) : -1);
+    uint32_t my_req = 0, my_local = 0;
+    const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor, &my_req, &my_local)
+                                   : (lane < nt ? fill_row_of(p, t0 + lane, &oor, &my_req, &my_local) : -1);
     if (oor && threadIdx.x < 32 && blockIdx.y == 0 && blockIdx.z == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
     const uint64_t per_side = (uint64_t)nt * rb;
     const uint64_t total = (uint64_t)(h1 - h0) * 2 * per_side;
@@ -740,12 +765,19 @@ cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &L, uin
                               cudaStream_t stream) {
   if (p.total_tokens == 0 || p.n_heads == 0 || n_layers == 0) return cudaSuccess;
   if (n_layers > kMaxFillLayers) return cudaErrorInvalidValue;
+  // rows from per-request values: one head per row, 16-byte rows and caches (the vectorised path)
+  if (p.req_src && (p.n_heads != 1 || !p.req_alloc || p.row_bytes % 16 ||
+                    ((reinterpret_cast<uint64_t>(L.cache_k[0]) | reinterpret_cast<uint64_t>(L.cache_v[0])) & 15u)))
+    return cudaErrorInvalidValue;
   // split the heads into groups only as far as needed for about two CTAs per SM
   const uint64_t sms = (uint64_t)sm_count();
   const uint64_t chunks = (p.total_tokens + kFillTokens - 1) / kFillTokens;
   uint64_t groups = (2 * sms + chunks * n_layers - 1) / (chunks * n_layers);
   groups = groups < 1 ? 1 : (groups > p.n_heads ? p.n_heads : groups);
-  paged_fill_kernel<<<dim3((unsigned)chunks, (unsigned)groups, n_layers), kFillThreads, 0, stream>>>(p, L);
+  if (p.req_src)
+    paged_fill_kernel<true><<<dim3((unsigned)chunks, (unsigned)groups, n_layers), kFillThreads, 0, stream>>>(p, L);
+  else
+    paged_fill_kernel<false><<<dim3((unsigned)chunks, (unsigned)groups, n_layers), kFillThreads, 0, stream>>>(p, L);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }

@@ -123,6 +123,14 @@ struct PagedFillParams {
   uint32_t n_heads, total_tokens, row_bytes, batch, max_blocks, num_blocks, block_size;
   unsigned int *out_of_range;        // optional: tokens skipped for a position or block out of range
                                      // (counted once per token, in the first layer)
+  // Optional source of rows per request instead of the packed k_fill / v_fill: request r's value
+  // (a raw-byte chunk blob) holds, for layer l, its K rows at req_src[r] + 2 l req_alloc[r] and its
+  // V rows req_alloc[r] further on, one row_bytes row per token (one head: n_heads must be 1, and
+  // row_bytes and the caches 16-byte aligned). req_src[r] already points past the value's header.
+  // A launch covers layers layer0 .. layer0 + n_layers - 1 (its z index adds to layer0).
+  const uint64_t *req_src;           // [batch] device addresses, or nullptr
+  const uint64_t *req_alloc;         // [batch] bytes of one K (or V) region of the request's value
+  uint32_t layer0;
 };
 
 constexpr uint32_t kMaxFillLayers = 64;

@@ -2223,6 +2223,184 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
   return KVS_OK;
 }
 
+// ---------------------------------------------------------------------------- chunk restore
+
+// Restore of n chunk values straight into a paged cache (kvs_restore_chunks in kvs.h): the catalog
+// decides every outcome in key order as a sequence of gets would (commit barrier, recency,
+// read-through admission); then one paged-fill launch per 64 layers reads each chunk's K / V rows
+// where the value lives -- its slab block, or its pinned host copy when no block could be
+// allocated or a later admission of the same call took the block again.
+static int restore_chunks_impl(kvs_client *c, uint32_t n, const void *const *keys, const uint32_t *key_lens,
+                               const uint32_t *tokens, uint32_t n_layers, void *const *cache_ks,
+                               void *const *cache_vs, uint32_t num_blocks, uint32_t block_size, uint32_t row_bytes,
+                               const int32_t *page_table, uint32_t max_blocks, const int32_t *start_positions,
+                               uint8_t *found, void *stream) {
+  const char *op = "restore_chunks";
+  if (n == 0) return KVS_OK;
+  if (!keys || !key_lens || !tokens || !cache_ks || !cache_vs || !page_table || !start_positions || !found)
+    return set_err(KVS_E_INVAL, "%s: null argument", op);
+  if (n_layers == 0 || block_size == 0 || max_blocks == 0 || num_blocks == 0)
+    return set_err(KVS_E_INVAL, "%s: n_layers, block_size, max_blocks_per_chunk and num_blocks must be > 0", op);
+  if (row_bytes == 0 || row_bytes % 16)
+    return set_err(KVS_E_INVAL, "%s: row_bytes %u must be a nonzero multiple of 16", op, row_bytes);
+  for (uint32_t i = 0; i < n; ++i) TRY(validate_key(c, keys[i], key_lens[i], op));
+  for (uint32_t l = 0; l < n_layers; ++l) {
+    if (((reinterpret_cast<uint64_t>(cache_ks[l]) | reinterpret_cast<uint64_t>(cache_vs[l])) & 15u) != 0)
+      return set_err(KVS_E_INVAL, "%s: cache tensors of layer %u must be 16-byte aligned", op, l);
+    TRY(check_device_ptr(c, cache_ks[l], op, "cache_k"));
+    TRY(check_device_ptr(c, cache_vs[l], op, "cache_v"));
+  }
+  // value layout of the raw-byte chunk codec: header [MAGIC, n_layers, 2 alloc x n_layers] padded
+  // to 32 bytes, then per layer K (alloc bytes) and V (alloc bytes)
+  const uint64_t hdr = 4ull * (((2ull + n_layers) + 7) / 8 * 8);
+  std::vector<uint64_t> alloc(n), vlen(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    alloc[i] = (uint64_t)((tokens[i] + block_size - 1) / block_size) * block_size * row_bytes;
+    vlen[i] = hdr + 2ull * n_layers * alloc[i];
+  }
+  const size_t ns = c->shards.size();
+  std::vector<uint8_t> inv(ns, 0);
+  std::vector<uint32_t> si(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    si[i] = shard_index(c, (const uint8_t *)keys[i], key_lens[i]);
+    inv[si[i]] = 1;
+  }
+  ShardLocks locks(involved_servers(c, inv));
+  TRY(quarantine_on_error(c, commit_barrier(c, inv)));
+  // every length is checked before any recency changes, as one failed get leaves the store as it was
+  std::vector<uint32_t> slot(n);
+  for (uint32_t i = 0; i < n; ++i) {
+    kvs_server *s = c->shards[si[i]];
+    slot[i] = s->dir->lookup((const uint8_t *)keys[i], key_lens[i]);
+    if (slot[i] != kvs::kBucketEmpty && s->dir->entry(slot[i]).total_len != vlen[i])
+      return set_err(KVS_E_FORMAT, "%s: stored value for key %u has length %llu, a %u-token chunk of %u layers needs %llu",
+                     op, i, (unsigned long long)s->dir->entry(slot[i]).total_len, tokens[i], n_layers,
+                     (unsigned long long)vlen[i]);
+  }
+  struct Src {
+    uint32_t i, shard, slot;
+    uint64_t slab;       // slab address the value is read from (0: its host copy)
+    uint64_t host_dev;   // device alias of the host copy
+    const uint8_t *host; // the host copy (admissions copy from it)
+    bool admit;          // the slab block is filled from the host copy first
+  };
+  std::vector<Src> src;
+  std::multimap<std::pair<uint32_t, uint32_t>, size_t> reads;  // (shard, slot) -> src entries on its block
+  for (size_t k = 0; k < ns; ++k)
+    if (inv[k]) c->shards[k]->dir->take_evicted();
+  for (uint32_t i = 0; i < n; ++i) {
+    found[i] = 0;
+    if (slot[i] == kvs::kBucketEmpty) continue;
+    kvs_server *s = c->shards[si[i]];
+    uint64_t off = 0;
+    const auto action = s->dir->get_hit(slot[i], &off);
+    // a block this call reads and a later admission just took: read that value's host copy
+    for (uint32_t ev : s->dir->take_evicted()) {
+      auto range = reads.equal_range({si[i], ev});
+      for (auto it = range.first; it != range.second; ++it) {
+        src[it->second].slab = 0;
+        src[it->second].admit = false;
+      }
+      reads.erase(range.first, range.second);
+    }
+    const HostBacking &hb = s->dir->backing(slot[i]);
+    Src r{i, si[i], slot[i], 0, s->device_alias(hb), s->host_ptr(hb), false};
+    if (action == Directory::GetAction::kDevice) {
+      r.slab = s->slab_base() + s->dir->entry(slot[i]).value_off;
+    } else if (action == Directory::GetAction::kAdmit) {
+      r.slab = s->slab_base() + off;
+      r.admit = true;
+      s->mprof.to_device_count++;
+      s->moves_completed.fetch_add(1, std::memory_order_relaxed);
+    } else {
+      s->mprof.to_device_count++;
+      s->moves_completed.fetch_add(1, std::memory_order_relaxed);
+    }
+    if (r.slab) reads.insert({{si[i], slot[i]}, src.size()});
+    found[i] = 1;
+    src.push_back(r);
+  }
+  for (const Src &r : src)
+    if (!r.slab && !r.host_dev)
+      return set_err(KVS_E_CUDA, "%s: the host copy of key %u has no device alias", op, r.i);
+  if (src.empty()) return KVS_OK;  // every key missed
+  const uint32_t nr = (uint32_t)src.size();
+  TRY(begin_op(c, stream));
+  Staging &st = c->stage;
+  TRY(st.begin(4096 + 32ull * nr + 4ull * nr * max_blocks, c->stream));
+  const size_t cu_off = st.take(4ull * (nr + 1)), pt_off = st.take(4ull * nr * max_blocks);
+  const size_t sp_off = st.take(4ull * nr), rs_off = st.take(8ull * nr), ra_off = st.take(8ull * nr);
+  int32_t *cu = st.h<int32_t>(cu_off);
+  cu[0] = 0;
+  uint64_t payload = 0, total = 0;
+  for (uint32_t k = 0; k < nr; ++k) {
+    const Src &r = src[k];
+    total += tokens[r.i];
+    if (total > 0x7FFFFFFFull) return set_err(KVS_E_INVAL, "%s: more than 2^31 tokens in one call", op);
+    cu[k + 1] = (int32_t)total;
+    std::memcpy(st.h<int32_t>(pt_off) + (uint64_t)k * max_blocks, page_table + (uint64_t)r.i * max_blocks,
+                4ull * max_blocks);
+    st.h<int32_t>(sp_off)[k] = start_positions[r.i];
+    st.h<uint64_t>(rs_off)[k] = (r.slab ? r.slab : r.host_dev) + hdr;
+    st.h<uint64_t>(ra_off)[k] = alloc[r.i];
+    payload += 2ull * n_layers * tokens[r.i] * row_bytes;
+  }
+  TRY(st.upload(c->stream, st.used));
+  for (size_t k = 0; k < ns; ++k)
+    if (inv[k]) TRY(chain_wait(c, c->shards[k]));
+  // read-through admissions first: host copy -> the value's new slab block
+  for (const Src &r : src)
+    if (r.admit && r.slab)
+      CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<void *>(r.slab), r.host, vlen[r.i], cudaMemcpyHostToDevice, c->stream));
+  kvs::PagedFillParams fp{};
+  fp.cu_seqlens = st.d<int32_t>(cu_off);
+  fp.page_table = st.d<int32_t>(pt_off);
+  fp.start_positions = st.d<int32_t>(sp_off);
+  fp.req_src = st.d<uint64_t>(rs_off);
+  fp.req_alloc = st.d<uint64_t>(ra_off);
+  fp.n_heads = 1;
+  fp.total_tokens = (uint32_t)total;
+  fp.row_bytes = row_bytes;
+  fp.batch = nr;
+  fp.max_blocks = max_blocks;
+  fp.num_blocks = num_blocks;
+  fp.block_size = block_size;
+  cudaEvent_t t0 = nullptr;
+  c->time_begin(&t0);
+  for (uint32_t l0 = 0; l0 < n_layers; l0 += kvs::kMaxFillLayers) {
+    const uint32_t nl = std::min<uint32_t>(kvs::kMaxFillLayers, n_layers - l0);
+    kvs::FillLayers L{};
+    for (uint32_t l = 0; l < nl; ++l) {
+      L.cache_k[l] = static_cast<uint8_t *>(cache_ks[l0 + l]);
+      L.cache_v[l] = static_cast<uint8_t *>(cache_vs[l0 + l]);
+    }
+    fp.layer0 = l0;
+    CUDA_TRY(kvs::launch_paged_fill(fp, L, nl, c->stream));
+  }
+  c->time_end(t0, 1, payload);
+  for (size_t k = 0; k < ns; ++k)
+    if (inv[k]) {
+      c->shards[k]->launches++;
+      TRY(chain_record(c, k));
+    }
+  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  TRY(check_tma_timeouts(c, op));
+  // no end_op: the client stream is idle after the synchronise
+  return KVS_OK;
+}
+
+int kvs_restore_chunks(kvs_client *c, uint32_t n, const void *const *keys, const uint32_t *key_lens,
+                       const uint32_t *tokens, uint32_t n_layers, void *const *cache_ks, void *const *cache_vs,
+                       uint32_t num_blocks, uint32_t block_size, uint32_t row_bytes, const int32_t *page_table,
+                       uint32_t max_blocks_per_chunk, const int32_t *start_positions, uint8_t *found, void *stream) {
+  TRY(check_client(c));
+  std::lock_guard<std::mutex> lk(c->mu);
+  DeviceGuard g(c->device);
+  return quarantine_on_error(c, restore_chunks_impl(c, n, keys, key_lens, tokens, n_layers, cache_ks, cache_vs,
+                                                    num_blocks, block_size, row_bytes, page_table,
+                                                    max_blocks_per_chunk, start_positions, found, stream));
+}
+
 int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const uint64_t *keys,
                    const int64_t *block_ids, uint8_t *found, void *stream) {
   TRY(check_client(c));

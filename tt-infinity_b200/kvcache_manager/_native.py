@@ -192,6 +192,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvs_put_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, P, P, C.c_int, P]),
     "kvs_get_blocks": (C.c_int, [P, C.POINTER(BlockLayout), C.c_uint32, P, P, P, P]),
     "kvs_exists_batch": (C.c_int, [P, C.c_uint32, P, P]),
+    "kvs_restore_chunks": (
+        C.c_int,
+        [P, C.c_uint32, C.POINTER(P), _u32p, _u32p, C.c_uint32, C.POINTER(P), C.POINTER(P), C.c_uint32, C.c_uint32,
+         C.c_uint32, C.POINTER(C.c_int32), C.c_uint32, C.POINTER(C.c_int32), _u8p, P],
+    ),
     "kvs_ipc_export": (C.c_int, [P, C.POINTER(IpcHandle), _u64p]),
     "kvs_ipc_open": (C.c_int, [C.c_int32, C.POINTER(IpcHandle), C.POINTER(P)]),
     "kvs_ipc_close": (C.c_int, [C.c_int32, P]),

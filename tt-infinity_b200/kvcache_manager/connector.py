@@ -32,6 +32,13 @@ from . import codec, ops
 from ._facade import Client
 
 
+def _stream_of(t: Any) -> int:
+    """Raw handle of the current stream on the tensor's device."""
+    import torch
+
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
 def kv_caches_from_vllm(kv_caches: Sequence[Any]) -> list:
     """vLLM CUDA caches (per layer ``[2, num_blocks, block_size, heads, head_dim]``) as per-layer
     ``(K, V)`` tensors whose first dimension is the block index (views, no copy)."""
@@ -145,6 +152,56 @@ class KVCacheClient:
         self.stats["get_bytes"] += int(plan["value_len"])
         return True
 
+    def get_chunks_device(self, keys: Sequence[str], kvcaches: Any, num_layers: int,
+                          slot_mapping_slices: Sequence[Any]) -> list[bool]:
+        """Restore several chunks in one store call: every chunk's rows go from where its value
+        lives straight into the caches, all layers in one fill launch (kvs_restore_chunks).
+        The reference fetches the chunks and fills one layer per call (TTGPUConnector's batched
+        restore, P5:6780-6870 with _paged_fill_layer_coalesced, P5:11563-11770). Returns found per
+        chunk; a missing chunk leaves its blocks untouched."""
+        import ctypes as C
+
+        import numpy as np
+
+        from . import _native
+
+        n = len(keys)
+        if n == 0:
+            return []
+        if len(slot_mapping_slices) != n:
+            raise ValueError("get_chunks_device: one slot mapping slice per key")
+        k0 = kvcaches[0][0]
+        bs = int(k0.shape[1])
+        if bs != self.raw_codec.block_size:
+            raise ValueError(f"cache blocks hold {bs} tokens, not block_size {self.raw_codec.block_size}")
+        row_bytes = int(k0[0, 0].numel() * k0.element_size())
+        slots = [self.raw_codec._chunk_slots(sl) for sl in slot_mapping_slices]
+        tokens = np.array([len(x) for x in slots], np.uint32)
+        max_blocks = int(max(-(-int(t) // bs) for t in tokens))
+        # a chunk starts on a block boundary with sequential slots: its blocks follow its first one
+        page = np.zeros((n, max_blocks), np.int32)
+        for i, x in enumerate(slots):
+            nb = -(-len(x) // bs)
+            page[i, :nb] = np.arange(x[0] // bs, x[0] // bs + nb, dtype=np.int32)
+        starts = np.zeros(n, np.int32)
+        raw = [self.raw_key(k) for k in keys]
+        key_arr = (C.c_void_p * n)(*[C.cast(C.c_char_p(b), C.c_void_p) for b in raw])
+        lens = np.array([len(b) for b in raw], np.uint32)
+        ks = (C.c_void_p * num_layers)(*[kvcaches[l][0].data_ptr() for l in range(num_layers)])
+        vs = (C.c_void_p * num_layers)(*[kvcaches[l][1].data_ptr() for l in range(num_layers)])
+        found = np.zeros(n, np.uint8)
+        _native.check(_native.load().kvs_restore_chunks(
+            self.client._handle(), n, key_arr, lens.ctypes.data_as(_native._u32p),
+            tokens.ctypes.data_as(_native._u32p), num_layers, ks, vs, int(k0.shape[0]), bs, row_bytes,
+            page.ctypes.data_as(C.POINTER(C.c_int32)), max_blocks, starts.ctypes.data_as(C.POINTER(C.c_int32)),
+            found.ctypes.data_as(_native._u8p), C.c_void_p(_stream_of(k0))))
+        hits = int(found.sum())
+        payload = int(sum(2 * num_layers * int(t) * row_bytes for t, f in zip(tokens, found) if f))
+        self.stats["gets"] += hits
+        self.stats["get_misses"] += n - hits
+        self.stats["get_bytes"] += payload
+        return [bool(f) for f in found]
+
     def wait_put_done(self, key: str) -> None:
         """Puts land before Client.put returns (write-through finishes asynchronously)."""
 
@@ -193,8 +250,20 @@ class GPUConnector:
             self.from_gpu(mo, s, e, **kwargs)
 
     def batched_to_gpu(self, memory_objs: List[Any], starts: List[int], ends: List[int], **kwargs: Any) -> None:
+        """Restore every announced chunk in one store call (KVCacheClient.get_chunks_device): one
+        fill launch writes all chunks into all layers, reading each chunk where the store holds it."""
+        keys, slices = [], []
         for mo, s, e in zip(memory_objs, starts, ends):
-            self.to_gpu(mo, s, e, **kwargs)
+            sl = self._slice(s, e, kwargs, "batched_to_gpu")
+            key = self.client.pop_pending_get(id(mo))
+            if key is None:
+                raise RuntimeError(
+                    f"GPUConnector.batched_to_gpu: no pending-get entry for id(memory_obj)={id(mo)}; "
+                    "RemoteConnector.get must run before batched_to_gpu")
+            keys.append(key.to_string())
+            slices.append(sl)
+        found = self.client.get_chunks_device(keys, self.kvcaches, self.num_layers, slices)
+        self.load_misses += sum(1 for f in found if not f)
 
     def get_shape(self, num_tokens: int):
         """Shape of one chunk as LMCache sizes it: [2, layers, tokens, hidden] of this rank."""
