@@ -64,7 +64,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-multiturn", action="store_true",
+    ap.add_argument("--no-extras", action="store_true",
                     help="N=1: skip the config-3 multi-turn and connector-restore runs that follow the main step")
     ap.add_argument("--latency-samples", type=int, default=200)
     ap.add_argument("--sweep", action="store_true",
@@ -1432,7 +1432,7 @@ def main():
             line = run_sharded(args, rank, local_rank, world)
         else:
             line = run_ours(args, rank, local_rank, world)
-            if world == 1 and line is not None and not args.no_multiturn:
+            if world == 1 and line is not None and not args.no_extras:
                 import torch
 
                 torch.cuda.empty_cache()

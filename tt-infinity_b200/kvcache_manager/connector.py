@@ -252,6 +252,9 @@ class GPUConnector:
     def batched_to_gpu(self, memory_objs: List[Any], starts: List[int], ends: List[int], **kwargs: Any) -> None:
         """Restore every announced chunk in one store call (KVCacheClient.get_chunks_device): one
         fill launch writes all chunks into all layers, reading each chunk where the store holds it."""
+        sm = kwargs.get("slot_mapping")
+        if sm is not None and getattr(getattr(sm, "device", None), "type", "cpu") != "cpu":
+            kwargs = dict(kwargs, slot_mapping=sm.cpu())  # one device-to-host read for the whole batch
         keys, slices = [], []
         for mo, s, e in zip(memory_objs, starts, ends):
             sl = self._slice(s, e, kwargs, "batched_to_gpu")
