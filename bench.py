@@ -82,6 +82,8 @@ def parse() -> argparse.Namespace:
                     help="sharded store: P2P stores over NVLink (default) or NCCL send/recv of packed values")
     ap.add_argument("--mix", action="store_true",
                     help="hash-sharded 70/30 get/put mix of 256-block batches, config-1 KV shape, both transports")
+    ap.add_argument("--latency", action="store_true",
+                    help="single-block get latency on the Qwen3-32B-shaped block from a small pool")
     ap.add_argument("--restore", action="store_true",
                     help="the connector's batched restore of a Qwen3-32B-shaped 8192-token prompt (64 layers)")
     ap.add_argument("--fill", action="store_true",
@@ -1333,7 +1335,8 @@ def run_restore(args):
             return self.s
 
     torch.cuda.set_device(0)
-    layers, nb, bs, tokens, chunk = (8 if args.small else LAYERS), POOL_BLOCKS, BLOCK_TOKENS, 8192, 256
+    layers, nb, bs, tokens, chunk = (8, 512, BLOCK_TOKENS, 8192, 256) if args.small else (LAYERS, POOL_BLOCKS,
+                                                                                         BLOCK_TOKENS, 8192, 256)
     g = torch.Generator(device="cuda")
     g.manual_seed(21)
     vllm = [torch.empty((2, nb, bs, HEADS, HEAD_DIM), dtype=torch.bfloat16, device="cuda").normal_(generator=g)
@@ -1401,10 +1404,64 @@ def run_restore(args):
             "parity": "byte compare of every restored block with the stored chunks (first call)"}
 
 
+def run_latency(args):
+    """Single-block get latency on the Qwen3-32B-shaped block (64 layers, 16 MiB values) from a small
+    pool: p50 / p99 wall time of Client.get_blocks of one committed, device-resident block (the
+    call returns once the block has landed), and the scatter kernel's own time from CUDA events."""
+    import torch
+
+    from kvcache_manager import Client, PagedLayout, Server, codec
+
+    torch.cuda.set_device(0)
+    pool, n = 64, 16
+    g = torch.Generator(device=0)
+    g.manual_seed(1)
+    kv = [tuple(torch.empty((pool, HEADS, BLOCK_TOKENS, HEAD_DIM), dtype=torch.bfloat16, device=0).normal_(generator=g)
+                for _ in range(2)) for _ in range(LAYERS)]
+    layout = PagedLayout.from_kv_caches(kv)
+    vlen = layout.value_bytes()
+    units = -(-vlen // UNIT_BYTES)
+    block_units = 1 << (units - 1).bit_length()
+    server = Server(0, max_keys=4 * n, heap_bytes=(n + 4) * block_units * UNIT_BYTES,
+                    host_pool_bytes=(n + 4) * units * UNIT_BYTES)
+    client = Client(0, server)
+    keys = np.array(codec.chained_block_hashes(5, n), np.uint64)
+    client.put_blocks(layout, keys, np.arange(n), sync_commit=True)
+    dst = np.arange(n, 2 * n)
+    for j in range(5):  # untimed
+        client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
+    lat = []
+    for i in range(args.latency_samples):
+        j = i % n
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ok = client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
+        lat.append((time.perf_counter() - t0) * 1e6)
+        assert ok.all()
+    client.set_kernel_timing(True)
+    for i in range(args.latency_samples):
+        client.get_blocks(layout, keys[i % n:i % n + 1], dst[i % n:i % n + 1])
+    sc = client.kernel_timing()["scatter"]
+    client.close()
+    server.close()
+    for t, blk in zip([t for p in kv for t in p][:4], range(4)):
+        if not torch.equal(t[dst[blk]].view(torch.int16), t[blk].view(torch.int16)):
+            raise RuntimeError("a restored block differs from its source")
+    lat.sort()
+    return {"latency": "one committed device-resident 16 MiB block per Client.get_blocks call (64 layers x K, V "
+                       "of 8 x 64 x 128 bf16), wall time from the call to its return",
+            "samples": len(lat), "p50_us": round(lat[len(lat) // 2], 2),
+            "p99_us": round(lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)], 2),
+            "scatter_kernel_avg_us": round(1000 * sc["total_ms"] / max(1, sc["launches"]), 2),
+            "scatter_note": "CUDA events around the launch on the client stream (includes the launch's own "
+                            "device-side overhead)"}
+
+
 def main():
     args = parse()
-    if args.sweep or args.multiturn or args.fill or args.restore:
-        run = run_sweep if args.sweep else run_multiturn if args.multiturn else run_fill if args.fill else run_restore
+    if args.sweep or args.multiturn or args.fill or args.restore or args.latency:
+        run = (run_sweep if args.sweep else run_multiturn if args.multiturn else run_fill if args.fill
+               else run_restore if args.restore else run_latency)
         print(json.dumps(run(args)))
         return
     rank, local_rank, world = dist_env()
