@@ -94,26 +94,33 @@ def pack_requests(world: int, cap: int, op: int, get_keys: np.ndarray, get_ids: 
                   put_keys: np.ndarray, put_ids: np.ndarray,
                   table: np.ndarray | None = None) -> tuple[np.ndarray, list, list]:
     """Request records [world, request_words(cap)] (record o goes to shard o) and, per owner, the
-    batch positions of its gets and of its puts (in batch order)."""
+    batch positions of its gets and of its puts (in batch order). The keys of both kinds are
+    hashed in one pass, then one stable sort by (kind, owner) places every key in its record."""
     rec = np.zeros((world, request_words(cap)), np.int64)
-    g_own = shard_of_u64(get_keys, world, table)
-    p_own = shard_of_u64(put_keys, world, table)
-    g_pos, p_pos = [], []
-    gk = np.asarray(get_keys, np.uint64).view(np.int64)
-    pk = np.asarray(put_keys, np.uint64).view(np.int64)
-    for o in range(world):
-        gi = np.flatnonzero(g_own == o)
-        pi = np.flatnonzero(p_own == o)
-        if gi.size > cap or pi.size > cap:
-            raise ValueError(f"sharded store: more than {cap} keys for one shard in a step")
-        r = rec[o]
-        r[0], r[1], r[2] = gi.size, pi.size, op
-        r[_HDR:_HDR + gi.size] = gk[gi]
-        r[_HDR + cap:_HDR + cap + gi.size] = np.asarray(get_ids, np.int64)[gi]
-        r[_HDR + 2 * cap:_HDR + 2 * cap + pi.size] = pk[pi]
-        r[_HDR + 3 * cap:_HDR + 3 * cap + pi.size] = np.asarray(put_ids, np.int64)[pi]
-        g_pos.append(gi)
-        p_pos.append(pi)
+    rec[:, 2] = op
+    gk = np.asarray(get_keys, np.uint64).reshape(-1)
+    pk = np.asarray(put_keys, np.uint64).reshape(-1)
+    ng = gk.size
+    keys = np.concatenate([gk, pk])
+    ids = np.concatenate([np.asarray(get_ids, np.int64).reshape(-1), np.asarray(put_ids, np.int64).reshape(-1)])
+    own = shard_of_u64(keys, world, table)
+    group = own.copy()
+    group[ng:] += world  # gets of shard o are group o, puts of shard o group world + o
+    order = np.argsort(group, kind="stable")
+    counts = np.bincount(group, minlength=2 * world)
+    if counts.size and counts.max() > cap:
+        raise ValueError(f"sharded store: more than {cap} keys for one shard in a step")
+    rec[:, 0], rec[:, 1] = counts[:world], counts[world:]
+    starts = np.cumsum(counts) - counts
+    g = group[order]
+    slot = np.arange(order.size) - starts[g]
+    o, kind = g % world, g // world
+    base = _HDR + 2 * cap * kind + slot
+    rec[o, base] = keys.view(np.int64)[order]
+    rec[o, base + cap] = ids[order]
+    ends = np.cumsum(counts)
+    g_pos = [order[starts[i]:ends[i]] for i in range(world)]
+    p_pos = [order[starts[world + i]:ends[world + i]] - ng for i in range(world)]
     return rec, g_pos, p_pos
 
 
