@@ -89,8 +89,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--fill", action="store_true",
                     help="token-granular paged fill: 8192 tokens of 4 requests into 64 layers' caches")
     ap.add_argument("--resident", type=int, default=0,
-                    help="--mix: resident blocks per GPU (default: 1M / N, at most 16384: the pinned host "
-                         "tier mirrors every resident block)")
+                    help="--mix: resident blocks per GPU (default: 1M / N, capped so that the pinned host "
+                         "tier, which mirrors every resident block, stays within 35%% of the host's available memory)")
     args = ap.parse_args()
     if args.small:
         global LAYERS, POOL_BLOCKS, BATCH_BLOCKS, BLOCK_PAYLOAD, WORKLOAD
@@ -796,6 +796,18 @@ MIX_BATCH, MIX_GETS = 256, 179  # 70 / 30 get / put
 MIX_PAYLOAD = 2 * MIX_LAYERS * MIX_HEADS * MIX_BT * MIX_DIM * 2  # 256 KiB
 
 
+def _host_bytes_available() -> int:
+    """MemAvailable of this host (0 if unknown)."""
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
 def _splitmix64(x: np.ndarray) -> np.ndarray:
     z = (x + np.uint64(0x9E3779B97F4A7C15)).astype(np.uint64)
     z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
@@ -823,7 +835,17 @@ def run_mix(args, rank, local_rank, world):
     vlen = layout.value_bytes()
     units = -(-vlen // UNIT_BYTES)
     block_units = 1 << (units - 1).bit_length()
-    R = args.resident or min((1 << 20) // world, 16384)
+    # config 4 asks for 1 M resident blocks over the N GPUs; every resident block also lives in its
+    # owner's pinned host tier, so the default takes 1 M / N per GPU up to a pinned budget of 35 % of
+    # the host memory available (shared by the N processes of the box)
+    want = (1 << 20) // world
+    avail = _host_bytes_available()
+    per_block_host = units * UNIT_BYTES
+    cap = int(0.35 * avail / world / per_block_host) if avail else 16384
+    R = args.resident or min(want, cap)
+    residency = {"requested_per_gpu": want, "host_available_bytes": avail, "pinned_budget": "35% of available / N",
+                 "pinned_bytes_per_gpu": R * per_block_host,
+                 "limited_by": "--resident" if args.resident else ("host memory" if cap < want else "none")}
     max_keys = R + R // 8 + 1024
     store = sharded.create(layout, max_batch=MIX_BATCH, transport="p2p", max_keys=max_keys,
                            heap_bytes=max_keys * block_units * UNIT_BYTES,
@@ -911,7 +933,7 @@ def run_mix(args, rank, local_rank, world):
         "config": {"workload": "hash-sharded-config1-kv-70-30-get-put-256blk", "layers": MIX_LAYERS,
                    "kv_heads": MIX_HEADS, "head_dim": MIX_DIM, "block_tokens": MIX_BT, "pool_blocks": MIX_POOL,
                    "bytes_per_block": MIX_PAYLOAD, "batch": f"{MIX_GETS} gets + {MIX_BATCH - MIX_GETS} puts per rank",
-                   "resident_blocks_per_gpu": R, "resident_blocks_total": R * world,
+                   "resident_blocks_per_gpu": R, "resident_blocks_total": R * world, "residency": residency,
                    "populate_s": round(t_pop, 2), "parallelism": f"hash-sharded store over {world} GPUs"},
         "transports": results,
         "concurrent_d2h_GBps_per_gpu": {"rank0": round(hw_mine, 2), "min": round(hw_min, 2),
