@@ -134,3 +134,21 @@ def test_oracle_is_not_importable_from_the_product():
         if p.suffix in (".py", ".cu", ".cuh", ".cpp", ".hpp", ".h"):
             assert "oracle" not in p.read_text().replace("oracles", ""), p
     assert os.path.exists(_native.LIB_PATH)
+
+
+def test_new_entry_points_check_their_arguments_without_a_device(lib):
+    # the chunk restore needs a client; a null handle fails before anything else
+    assert lib.kvs_restore_chunks(None, 1, None, None, None, 1, None, None, 8, 16, 256, None, 1, None, None,
+                                  None) == _native.E_INVAL
+    assert b"client handle is null" in lib.kvs_last_error()
+    # copy-engine health: null outputs are refused, and the wait limit takes at most 2^32 - 1 polls
+    unsafe = C.c_uint32()
+    assert lib.kvs_copy_engine_status(0, None, C.byref(unsafe)) == _native.E_INVAL
+    assert lib.kvs_set_copy_wait_limit(1 << 33) == _native.E_INVAL
+    assert b"2^32 - 1" in lib.kvs_last_error()
+    assert lib.kvs_set_copy_wait_limit(-1) == 0  # the default
+    # timing calls need their handles
+    t = _native.KernelTiming()
+    assert lib.kvs_server_set_timing(None, 1) == _native.E_INVAL
+    assert lib.kvs_server_write_through_timing(None, C.byref(t)) == _native.E_INVAL
+    assert lib.kvs_client_host_tier_timing(None, C.byref(t), C.byref(t)) == _native.E_INVAL

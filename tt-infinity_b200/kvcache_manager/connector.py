@@ -138,19 +138,10 @@ class KVCacheClient:
         return True
 
     def get_chunk_device(self, key: str, kvcaches: Any, num_layers: int, slot_mapping_slice: Any) -> bool:
-        """Fetch the chunk's blob and scatter it into the live caches; False on a miss."""
-        plan = self._plan(kvcaches, num_layers, slot_mapping_slice)
-        members = plan["members"]
-        blob = self._blob_tensor(int(plan["value_len"]), members[0].device)
-        view = blob.view(-1)[: (int(plan["value_len"]) + 3) // 4]
-        if not self.client.get(self.raw_key(key), view):
-            self.stats["get_misses"] += 1
-            return False
-        ops.unpack_local_shards(view, members, plan["block_ids"], int(plan["shard_block_bytes"]),
-                                plan["region_bases"], blocking=False)
-        self.stats["gets"] += 1
-        self.stats["get_bytes"] += int(plan["value_len"])
-        return True
+        """Restore one chunk into the live caches; False on a miss. The reference gets the chunk's
+        blob and scatters it (P5:9710-9760); here the chunk's rows go from the store straight into
+        the caches (get_chunks_device), one copy instead of two."""
+        return self.get_chunks_device([key], kvcaches, num_layers, [slot_mapping_slice])[0]
 
     def get_chunks_device(self, keys: Sequence[str], kvcaches: Any, num_layers: int,
                           slot_mapping_slices: Sequence[Any]) -> list[bool]:
