@@ -266,6 +266,32 @@ def step_split(elapsed_ms, steps, gather, scatter, wt):
             "note": "rest = lookups, replica updates, host catalog work and the ordering between them"}
 
 
+def _native_lib():
+    from kvcache_manager import _native
+
+    return _native.load()
+
+
+def one_block_get_latency(torch, client, layout, keys, dst, samples):
+    """p50 / p99 in ms of Client.get_blocks of one committed device-resident block, from the call
+    to its return (the block has landed: get_blocks synchronises its own work), 5 untimed calls
+    first; keys[j] is restored into dst[j]."""
+    n = len(keys)
+    for j in range(5):  # untimed: the first calls size the staging areas
+        client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
+    lat = []
+    for i in range(samples):
+        j = i % n
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        ok = client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
+        lat.append((time.perf_counter() - t1) * 1e3)
+        torch.cuda.synchronize()
+        assert ok.all()
+    lat.sort()
+    return lat[len(lat) // 2], lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)]
+
+
 def run_ours(args, rank, local_rank, world):
     import torch
     import torch.distributed as dist
@@ -362,25 +388,15 @@ def run_ours(args, rank, local_rank, world):
         e2e_s = float(t.item())
     e2e = world * args.steps * step_bytes / e2e_s / GB
 
-    # ---- p50 / p99 get latency per block (committed, device-resident blocks)
-    lat = []
+    # ---- p50 / p99 get latency per block (committed, device-resident blocks): with the default
+    # engine choice (one-wave engine for a one-block copy), then with the persistent bulk engine
     keys, src, dst = step_inputs(9999)
     client.put_blocks(layout, keys, src, sync_commit=True)
-    for j in range(5):  # untimed: the first calls after the put size the staging areas
-        client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
-    for i in range(args.latency_samples):
-        j = i % BATCH_BLOCKS
-        torch.cuda.synchronize()
-        t1 = time.perf_counter()
-        # get_blocks returns once the block has landed in the pool (it synchronises its own work
-        # to read the lookup results); the caller's stream is ordered after it
-        ok = client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
-        lat.append((time.perf_counter() - t1) * 1e3)
-        torch.cuda.synchronize()
-        assert ok.all()
-    lat.sort()
-    p50 = lat[len(lat) // 2]
-    p99 = lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)]
+    p50, p99 = one_block_get_latency(torch, client, layout, keys, dst, args.latency_samples)
+    lib = _native_lib()
+    lib.kvs_set_small_copy_limit(0)
+    p50_bulk, p99_bulk = one_block_get_latency(torch, client, layout, keys, dst, args.latency_samples)
+    lib.kvs_set_small_copy_limit(-1)
 
     # ---- PCIe copy peaks (pinned, 1 GiB, best of 3): device->host bounds the write-through,
     # host->device the host-tier admissions
@@ -454,7 +470,9 @@ def run_ours(args, rank, local_rank, world):
         "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
                                      "samples": len(lat),
                                      "note": "one committed device-resident block per Client.get_blocks call, "
-                                             "timed from the call to its return (the block has landed)"},
+                                             "timed from the call to its return (the block has landed)",
+                                     "engine": "one-wave copy (copies up to 64 MiB)",
+                                     "bulk_engine": {"p50": round(p50_bulk, 4), "p99": round(p99_bulk, 4)}},
         "store": {k: stats[k] for k in ("writes_through", "victims_evicted", "catalog_replacements", "live_keys")},
         "clocks": clocks,
     }
@@ -1429,10 +1447,13 @@ def run_restore(args):
 def run_latency(args):
     """Single-block get latency on the Qwen3-32B-shaped block (64 layers, 16 MiB values) from a small
     pool: p50 / p99 wall time of Client.get_blocks of one committed, device-resident block (the
-    call returns once the block has landed), and the scatter kernel's own time from CUDA events."""
+    call returns once the block has landed) and the scatter kernel's own time from CUDA events,
+    with the one-wave engine (the default for a one-block copy) and with the bulk engine; then the
+    same call through the C ABI alone (ctypes with prepared addresses), the Python facade's share."""
     import torch
 
     from kvcache_manager import Client, PagedLayout, Server, codec
+    from kvcache_manager import _facade
 
     torch.cuda.set_device(0)
     pool, n = 64, 16
@@ -1450,33 +1471,48 @@ def run_latency(args):
     keys = np.array(codec.chained_block_hashes(5, n), np.uint64)
     client.put_blocks(layout, keys, np.arange(n), sync_commit=True)
     dst = np.arange(n, 2 * n)
-    for j in range(5):  # untimed
-        client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
+    lib = _native_lib()
+    out = {"latency": "one committed device-resident 16 MiB block per Client.get_blocks call (64 layers x K, V "
+                      "of 8 x 64 x 128 bf16), wall time from the call to its return",
+           "samples": args.latency_samples}
+    for name, limit in (("one_wave", -1), ("bulk", 0)):
+        lib.kvs_set_small_copy_limit(limit)
+        p50, p99 = one_block_get_latency(torch, client, layout, keys, dst, args.latency_samples)
+        client.set_kernel_timing(True)
+        for i in range(args.latency_samples):
+            client.get_blocks(layout, keys[i % n:i % n + 1], dst[i % n:i % n + 1])
+        sc = client.kernel_timing()["scatter"]
+        client.set_kernel_timing(False)
+        out[name] = {"p50_us": round(1e3 * p50, 2), "p99_us": round(1e3 * p99, 2),
+                     "scatter_kernel_avg_us": round(1000 * sc["total_ms"] / max(1, sc["launches"]), 2)}
+    lib.kvs_set_small_copy_limit(-1)
+    # the C ABI call alone: addresses and the stream handle prepared once
+    found = np.zeros(1, np.bool_)
+    k_addr = [_facade._addr(keys[j:j + 1]) for j in range(n)]
+    ids = dst.astype(np.int64)
+    b_addr = [_facade._addr(ids[j:j + 1]) for j in range(n)]
+    f_addr, h, ref = _facade._addr(found), client._handle(), layout.ref
+    stream = _facade._stream_handle(0)
     lat = []
-    for i in range(args.latency_samples):
+    for i in range(args.latency_samples + 5):
         j = i % n
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        ok = client.get_blocks(layout, keys[j:j + 1], dst[j:j + 1])
-        lat.append((time.perf_counter() - t0) * 1e6)
-        assert ok.all()
-    client.set_kernel_timing(True)
-    for i in range(args.latency_samples):
-        client.get_blocks(layout, keys[i % n:i % n + 1], dst[i % n:i % n + 1])
-    sc = client.kernel_timing()["scatter"]
+        rc = lib.kvs_get_blocks(h, ref, 1, k_addr[j], b_addr[j], f_addr, stream)
+        if i >= 5:
+            lat.append((time.perf_counter() - t0) * 1e6)
+        assert rc == 0 and found[0]
+    lat.sort()
+    out["c_abi_call"] = {"p50_us": round(lat[len(lat) // 2], 2),
+                         "note": "kvs_get_blocks through ctypes with prepared arguments, one-wave engine"}
     client.close()
     server.close()
     for t, blk in zip([t for p in kv for t in p][:4], range(4)):
         if not torch.equal(t[dst[blk]].view(torch.int16), t[blk].view(torch.int16)):
             raise RuntimeError("a restored block differs from its source")
-    lat.sort()
-    return {"latency": "one committed device-resident 16 MiB block per Client.get_blocks call (64 layers x K, V "
-                       "of 8 x 64 x 128 bf16), wall time from the call to its return",
-            "samples": len(lat), "p50_us": round(lat[len(lat) // 2], 2),
-            "p99_us": round(lat[min(len(lat) - 1, math.ceil(0.99 * len(lat)) - 1)], 2),
-            "scatter_kernel_avg_us": round(1000 * sc["total_ms"] / max(1, sc["launches"]), 2),
-            "scatter_note": "CUDA events around the launch on the client stream (includes the launch's own "
-                            "device-side overhead)"}
+    out["scatter_note"] = "CUDA events around the launch on the client stream (includes the launch's own " \
+                          "device-side overhead)"
+    return out
 
 
 def main():

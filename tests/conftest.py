@@ -42,3 +42,15 @@ def pytest_collection_modifyitems(config, items):
 @pytest.fixture(scope="session")
 def golden_dir() -> Path:
     return GOLDEN
+
+
+@pytest.fixture(params=["one_wave", "persistent"])
+def copy_engine(request):
+    """Runs a GPU test twice: with every copy whose grid allows it on the one-wave engine, and with
+    every copy on the persistent engines (bulk or LDG), so each engine is checked on the same cases."""
+    from kvcache_manager import _native
+
+    lib = _native.load()
+    assert lib.kvs_set_small_copy_limit(1 << 62 if request.param == "one_wave" else 0) == 0
+    yield request.param
+    assert lib.kvs_set_small_copy_limit(-1) == 0

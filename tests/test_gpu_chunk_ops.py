@@ -9,7 +9,7 @@ import torch
 
 from oracle import kvs_oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("copy_engine")]
 
 
 def _members(seed0, n_members, chips, wpm):

@@ -9,7 +9,8 @@ them, with the full limit, before it exits). These tests check what a caller see
     from every call after it (the reference's Quarantined state,
     src/client_operations_adapter.cpp:54-59), while a fresh client on the same shard still
     restores earlier puts bit-exactly.
-The limit is restored after each test.
+The copies stay on the bulk engine (the one-wave engine has no waits), and both limits are
+restored after each test.
 """
 
 import ctypes as C
@@ -28,8 +29,11 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture
 def lib():
     lib = _native.load()
+    # the bounded waits belong to the bulk engine: keep these small copies off the one-wave engine
+    assert lib.kvs_set_small_copy_limit(0) == 0
     yield lib
     assert lib.kvs_set_copy_wait_limit(-1) == 0
+    assert lib.kvs_set_small_copy_limit(-1) == 0
 
 
 def _status(lib, device=0):

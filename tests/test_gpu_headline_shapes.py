@@ -19,7 +19,7 @@ import torch
 from kvcache_manager import Client, PagedLayout, Server, codec
 from oracle import kvs_oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("copy_engine")]
 
 U = 4288
 

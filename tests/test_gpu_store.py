@@ -12,7 +12,7 @@ import torch
 from kvcache_manager import Client, KvsError, PagedLayout, Server, codec
 from oracle import kvs_oracle as O
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("copy_engine")]
 
 U = 4288
 LOC = {0: "device", 1: "host", 2: "pending", -1: "absent"}

@@ -152,3 +152,24 @@ def test_new_entry_points_check_their_arguments_without_a_device(lib):
     assert lib.kvs_server_set_timing(None, 1) == _native.E_INVAL
     assert lib.kvs_server_write_through_timing(None, C.byref(t)) == _native.E_INVAL
     assert lib.kvs_client_host_tier_timing(None, C.byref(t), C.byref(t)) == _native.E_INVAL
+
+
+def test_fastcall_module_is_bound_and_takes_only_exact_arrays(lib):
+    """The CPython module of the block calls is built beside the library and bound to it. It calls
+    the C ABI only with 1-D uint64 keys and int64 block ids of equal length (else NotImplemented,
+    and the facade converts); a failing call comes back as the library's error code."""
+    import numpy as np
+
+    fast = _native.fastcall
+    assert fast is not None, "the _fastcall module was not built or not bound"
+    keys, ids = np.arange(3, dtype=np.uint64), np.arange(3, dtype=np.int64)
+    assert fast.get_blocks(0, 0, keys, ids, 0) == _native.E_INVAL  # null client: checked before any device work
+    assert "client handle is null" in lib.kvs_last_error().decode()
+    assert fast.put_blocks(0, 0, keys, ids, False, 0) == _native.E_INVAL
+    assert fast.exists_batch(0, keys) == _native.E_INVAL
+    assert fast.get_blocks(0, 0, keys.astype(np.int64), ids, 0) is NotImplemented
+    assert fast.get_blocks(0, 0, keys, ids.astype(np.int32), 0) is NotImplemented
+    assert fast.get_blocks(0, 0, keys, ids[:2], 0) is NotImplemented
+    assert fast.get_blocks(0, 0, [1, 2, 3], ids, 0) is NotImplemented
+    assert fast.get_blocks(0, 0, keys[::2], ids[:2], 0) is NotImplemented  # not contiguous
+    assert fast.exists_batch(0, keys.reshape(1, 3)) is NotImplemented

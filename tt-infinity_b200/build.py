@@ -33,7 +33,38 @@ def needs_build(out: Path) -> bool:
     return any(p.stat().st_mtime > t for p in deps)
 
 
+FAST_SRC = CSRC / "pyext" / "kvs_fastcall.c"
+
+
+def fastcall_path() -> Path:
+    import sysconfig
+
+    return PKG / "kvcache_manager" / ("_fastcall" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_fastcall(force: bool = False) -> Path:
+    """The CPython module of the block calls' hot path (gcc; it calls the library through
+    function pointers, so it does not link against it)."""
+    import sysconfig
+
+    import numpy as np
+
+    out = fastcall_path()
+    if not force and out.exists() and out.stat().st_mtime > FAST_SRC.stat().st_mtime:
+        return out
+    cc = os.environ.get("CC", "gcc")
+    cmd = [cc, "-O2", "-shared", "-fPIC", "-Wall", "-I", sysconfig.get_paths()["include"], "-I", np.get_include(),
+           str(FAST_SRC), "-o", str(out) + ".tmp"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("gcc failed building the _fastcall module")
+    os.replace(str(out) + ".tmp", out)
+    return out
+
+
 def build(debug: bool = False, verbose: bool = False, force: bool = False) -> Path:
+    build_fastcall(force)
     if not force and not needs_build(OUT):
         return OUT
     flags = ARCH + [

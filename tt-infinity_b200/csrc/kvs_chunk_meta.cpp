@@ -166,10 +166,18 @@ ChunkCopyParams chunk_params(const ChunkArgs &a, const ChunkMeta &m, const uint8
   p.tiles_per_combo = m.tiles_per_combo;
   p.total_tiles = (uint64_t)a.n_blocks * a.n_ranks * m.tiles_per_combo;
   p.to_blob = a.to_blob;
+  uint64_t mx = 0, sum = 0;
+  for (uint32_t mi = 0; mi < a.n_members; ++mi) {
+    mx = a.member_block_bytes[mi] > mx ? a.member_block_bytes[mi] : mx;
+    sum += a.member_block_bytes[mi];
+  }
+  p.max_member_bytes = mx;
+  p.payload_bytes = sum * a.n_blocks * a.n_ranks;
   return p;
 }
 
 cudaError_t launch_chunk(const ChunkCopyParams &p, cudaStream_t stream) {
+  if (small_copy_suits(p)) return launch_chunk_copy_small(p, stream);
   if (bulk_engine_enabled()) return launch_chunk_copy_tma(p, stream);
   return launch_chunk_copy(p, stream);
 }

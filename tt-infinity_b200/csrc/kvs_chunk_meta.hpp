@@ -52,8 +52,9 @@ void pack_chunk_meta(const ChunkArgs &a, const ChunkMeta &m, uint8_t *image);
 // Copy-engine parameters whose arrays are the image at device address `meta`.
 ChunkCopyParams chunk_params(const ChunkArgs &a, const ChunkMeta &m, const uint8_t *meta);
 
-// Launches the copy with the runtime's engine choice: the bulk engine (both sides are device
-// memory here), or 16-byte loads and stores when KVS_COPY_ENGINE=ldg.
+// Launches the copy with the runtime's engine choice: the one-wave engine for copies of at most
+// small_copy_limit() bytes, else the bulk engine (both sides are device memory here), or 16-byte
+// loads and stores when KVS_COPY_ENGINE=ldg.
 cudaError_t launch_chunk(const ChunkCopyParams &p, cudaStream_t stream);
 
 // Engine choice shared with the store runtime.

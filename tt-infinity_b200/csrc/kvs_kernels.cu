@@ -2,6 +2,7 @@
 #include "kvs_kernels.cuh"
 
 #include <atomic>
+#include <cstdlib>
 
 namespace kvs {
 
@@ -116,6 +117,69 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const __grid_c
       cta_copy(blob_at, member, len);
     else
       cta_copy(member, blob_at, len);
+  }
+}
+
+// ---------------------------------------------------------------- one-wave small-copy engine
+//
+// A copy of a few MiB (one 16 MiB block) leaves a persistent grid only a few tiles per SM, so
+// its time is the ramp and tail of each CTA's pipeline, not bandwidth. This engine gives every
+// 16 KiB piece of every (blob block, rank, member) its own CTA -- grid (piece, member, combo) --
+// so the member is blockIdx.y and nothing is searched; each thread issues its four 16-byte loads
+// before any store, so the whole copy is in flight at once (one-block Qwen3 scatter: 12.7 us
+// between CUDA events against 15.6 us for the bulk engine, same B200).
+
+constexpr int kSmallThreads = 256;
+constexpr int kSmallWords = 4;  // 16-byte words per thread
+constexpr uint32_t kSmallPiece = (uint32_t)kSmallThreads * kSmallWords * 16u;  // 16 KiB
+constexpr uint64_t kSmallMaxCtas = 1u << 16;
+
+__global__ void __launch_bounds__(kSmallThreads) chunk_copy_small_kernel(const __grid_constant__ ChunkCopyParams p) {
+  const uint32_t m = blockIdx.y;
+  const uint32_t combo = blockIdx.z;
+  const uint32_t rk = combo % p.n_ranks;
+  const uint32_t bc = combo / p.n_ranks;
+  const uint32_t cb = bc % p.blocks_per_blob, blob = bc / p.blocks_per_blob;
+  const uint64_t blob_base = blob_ptr(p, blob);
+  if (!blob_base) return;
+  if (p.to_blob && p.n_header_words && blockIdx.x == 0 && m == 0 && cb == 0 && rk == 0)
+    for (uint32_t w = threadIdx.x; w < p.n_header_words; w += kSmallThreads)
+      reinterpret_cast<uint32_t *>(blob_base)[w] = p.header_words[w];
+  // the three layout loads are independent: one round trip
+  const uint64_t sbb = __ldg(p.member_bytes + m);
+  const uint64_t mp = __ldg(p.member_ptrs + member_index(p, blob, rk, m));
+  const uint64_t rb = __ldg(p.region_bases + m);
+  const uint64_t seg_off = (uint64_t)blockIdx.x * kSmallPiece;
+  if (seg_off >= sbb) return;
+  const uint64_t len = sbb - seg_off < kSmallPiece ? sbb - seg_off : kSmallPiece;
+  const int64_t block = block_id(p, (uint64_t)blob * p.blocks_per_blob + cb);
+  uint8_t *member = reinterpret_cast<uint8_t *>(mp) + (uint64_t)block * sbb + seg_off;
+  uint8_t *blob_at = reinterpret_cast<uint8_t *>(blob_base) + rb + (uint64_t)cb * sbb * p.n_ranks +
+                     (uint64_t)rk * sbb + seg_off;
+  const uint8_t *src = p.to_blob ? member : blob_at;
+  uint8_t *dst = p.to_blob ? blob_at : member;
+  const uint64_t align = reinterpret_cast<uint64_t>(dst) | reinterpret_cast<uint64_t>(src) | len;
+  const uint32_t tid = threadIdx.x;
+  if ((align & 15u) == 0) {
+    const int4 *s = reinterpret_cast<const int4 *>(src);
+    int4 *d = reinterpret_cast<int4 *>(dst);
+    const uint32_t n = (uint32_t)(len >> 4);
+    int4 v[kSmallWords];
+#pragma unroll
+    for (int u = 0; u < kSmallWords; ++u) {
+      const uint32_t i = tid + u * kSmallThreads;
+      if (i < n) v[u] = ld_stream(s + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kSmallWords; ++u) {
+      const uint32_t i = tid + u * kSmallThreads;
+      if (i < n) d[i] = v[u];
+    }
+  } else if ((align & 3u) == 0) {
+    for (uint32_t i = tid; i < (uint32_t)(len >> 2); i += kSmallThreads)
+      reinterpret_cast<uint32_t *>(dst)[i] = reinterpret_cast<const uint32_t *>(src)[i];
+  } else {
+    for (uint32_t i = tid; i < (uint32_t)len; i += kSmallThreads) dst[i] = src[i];
   }
 }
 
@@ -727,6 +791,44 @@ cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream)
   ChunkCopyParams q = p;
   q.wait_polls = g_wait_polls.load(std::memory_order_relaxed);
   chunk_copy_tma_kernel<<<(unsigned)grid, kTmaThreads, kTmaSmem, stream>>>(q);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+namespace {
+uint64_t env_small_limit() {
+  const char *v = std::getenv("KVS_SMALL_COPY_BYTES");
+  if (!v || !*v) return 64ull << 20;
+  char *end = nullptr;
+  const unsigned long long x = std::strtoull(v, &end, 10);
+  return (end && *end == '\0') ? (uint64_t)x : (64ull << 20);
+}
+std::atomic<uint64_t> g_small_limit{env_small_limit()};
+
+dim3 small_grid(const ChunkCopyParams &p) {
+  const uint64_t pieces = (p.max_member_bytes + kSmallPiece - 1) / kSmallPiece;
+  const uint64_t combos = (uint64_t)p.n_blobs * p.blocks_per_blob * p.n_ranks;
+  return dim3((unsigned)pieces, p.n_members, (unsigned)combos);
+}
+}  // namespace
+
+uint64_t small_copy_limit() { return g_small_limit.load(std::memory_order_relaxed); }
+void set_small_copy_limit(uint64_t bytes) { g_small_limit.store(bytes, std::memory_order_relaxed); }
+
+bool small_copy_suits(const ChunkCopyParams &p) {
+  if (!p.max_member_bytes || !p.payload_bytes || p.payload_bytes > small_copy_limit()) return false;
+  const uint64_t pieces = (p.max_member_bytes + kSmallPiece - 1) / kSmallPiece;
+  const uint64_t combos = (uint64_t)p.n_blobs * p.blocks_per_blob * p.n_ranks;
+  if (p.n_members == 0 || p.n_members > 65535 || combos == 0 || combos > 65535) return false;
+  return pieces * p.n_members * combos <= kSmallMaxCtas;
+}
+
+cudaError_t launch_chunk_copy_small(const ChunkCopyParams &p, cudaStream_t stream) {
+  if (p.total_tiles == 0 && (p.n_header_words == 0 || !p.to_blob)) return cudaSuccess;
+  if (!inline_ids_fit(p) || !p.max_member_bytes) return cudaErrorInvalidValue;
+  const dim3 grid = small_grid(p);
+  if (grid.y == 0 || grid.y > 65535 || grid.z == 0 || grid.z > 65535) return cudaErrorInvalidValue;
+  chunk_copy_small_kernel<<<grid, kSmallThreads, 0, stream>>>(p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }

@@ -79,6 +79,10 @@ struct ChunkCopyParams {
   uint32_t wait_polls;       // polls of one bounded wait on a tile load (set by the launcher)
   int64_t inline_ids[kInlineKeys];  // block ids when block_ids is nullptr (n_blobs * blocks_per_blob <= 8)
   uint64_t inline_blobs[kInlineKeys];  // blob addresses when blob_ptrs is nullptr (n_blobs <= 8)
+  // Host-side facts for the engine choice (no kernel reads them; 0 = not given, which keeps the
+  // persistent engines): the largest member block in bytes, and the bytes the launch moves.
+  uint64_t max_member_bytes;
+  uint64_t payload_bytes;
 };
 
 struct LookupParams {
@@ -144,6 +148,15 @@ struct FillLayers {  // by value in the kernel parameters (2 KiB)
 cudaError_t launch_chunk_copy(const ChunkCopyParams &p, cudaStream_t stream, int grid_ctas = 0);
 // TMA bulk-copy variant (sources and destinations in device memory, this GPU's or a peer's).
 cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream);
+// One-wave variant for small copies: one CTA per 16 KiB of each (blob block, rank, member), every
+// thread's loads issued before its stores, no tile walk. Needs p.max_member_bytes.
+cudaError_t launch_chunk_copy_small(const ChunkCopyParams &p, cudaStream_t stream);
+// Whether a copy goes to the one-wave variant: its facts are given, it moves at most
+// small_copy_limit() bytes, and its grid stays small. small_copy_limit() is 64 MiB unless
+// KVS_SMALL_COPY_BYTES sets it (0 turns the variant off); set_small_copy_limit overrides both.
+bool small_copy_suits(const ChunkCopyParams &p);
+uint64_t small_copy_limit();
+void set_small_copy_limit(uint64_t bytes);
 // Counters of the bulk-copy engine on the current device (both 0 in normal operation): bounded
 // waits on a tile load that expired, and CTAs that exited while one of their loads still had not
 // landed after the full wait limit (the engine cannot be trusted after that).

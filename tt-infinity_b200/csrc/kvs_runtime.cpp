@@ -546,15 +546,30 @@ struct kvs_client {
 
 namespace {
 
-// Copy-engine choice: the TMA bulk engine for device memory (this GPU's or a peer's), the
-// LDG/STG engine when a side is host memory. KVS_COPY_ENGINE=ldg forces the LDG engine.
+// Copy-engine choice: the one-wave engine for copies of at most a few MiB whose layout facts
+// the caller gave (max_member_bytes, payload_bytes), else the TMA bulk engine for device memory
+// (this GPU's or a peer's) and the LDG/STG engine when a side is host memory.
+// KVS_COPY_ENGINE=ldg forces the LDG engine for the copies that do not take the one-wave engine.
 bool tma_enabled() { return kvs::bulk_engine_enabled(); }
 
 cudaError_t launch_copy(kvs::ChunkCopyParams p, cudaStream_t stream, bool device_memory_only,
                         unsigned int *timeout_flag) {
   p.timeout_flag = timeout_flag;
+  if (kvs::small_copy_suits(p)) return kvs::launch_chunk_copy_small(p, stream);
   if (device_memory_only && tma_enabled()) return kvs::launch_chunk_copy_tma(p, stream);
   return kvs::launch_chunk_copy(p, stream);
+}
+
+// Sets the engine-choice facts of a copy of `combos` (blob block, rank) pairs over a layout whose
+// member blocks are `member_bytes[0..n_members)`.
+void set_copy_facts(kvs::ChunkCopyParams *p, const uint64_t *member_bytes, uint32_t n_members, uint64_t combos) {
+  uint64_t mx = 0, sum = 0;
+  for (uint32_t m = 0; m < n_members; ++m) {
+    mx = member_bytes[m] > mx ? member_bytes[m] : mx;
+    sum += member_bytes[m];
+  }
+  p->max_member_bytes = mx;
+  p->payload_bytes = sum * combos;
 }
 
 // Bounded waits in the bulk engine that expired (never in normal operation) turn into an error.
@@ -867,6 +882,7 @@ int flush_puts(PutBatch &b, cudaStream_t) {
       p.tiles_per_combo = b.fmt->tile_prefix.back();
       p.total_tiles = (uint64_t)n * p.tiles_per_combo;
       p.to_blob = 1;
+      set_copy_facts(&p, b.layout->member_block_bytes, b.layout->n_members, n);
       cudaEvent_t timed_start = nullptr;
       c->time_begin(&timed_start);
       CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
@@ -889,6 +905,7 @@ int flush_puts(PutBatch &b, cudaStream_t) {
         p.tiles_per_combo = (b.items[i].len + kTileBytes - 1) / kTileBytes;
         p.total_tiles = p.tiles_per_combo;
         p.to_blob = 1;
+        set_copy_facts(&p, &b.items[i].len, 1, 1);
         CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
       }
     }
@@ -991,6 +1008,7 @@ int launch_value_copy(kvs_client *c, size_t rec_off, uint64_t len, bool device_m
   p.tiles_per_combo = (len + kTileBytes - 1) / kTileBytes;
   p.total_tiles = p.tiles_per_combo;
   p.to_blob = 0;
+  if (device_memory_only) set_copy_facts(&p, &len, 1, 1);
   CUDA_TRY(launch_copy(p, c->stream, device_memory_only, c->timeout_flag));
   return KVS_OK;
 }
@@ -1042,6 +1060,12 @@ int kvs_copy_engine_status(int32_t device, uint32_t *expired_waits, uint32_t *un
 int kvs_set_copy_wait_limit(int64_t polls) {
   if (polls > (int64_t)UINT32_MAX) return set_err(KVS_E_INVAL, "copy wait limit %lld exceeds 2^32 - 1 polls", (long long)polls);
   kvs::set_copy_wait_polls(polls < 0 ? kvs::default_copy_wait_polls() : (uint32_t)polls);
+  return KVS_OK;
+}
+
+int kvs_set_small_copy_limit(int64_t bytes) {
+  static const uint64_t initial = kvs::small_copy_limit();  // the default or KVS_SMALL_COPY_BYTES
+  kvs::set_small_copy_limit(bytes < 0 ? initial : (uint64_t)bytes);
   return KVS_OK;
 }
 
@@ -1877,6 +1901,7 @@ static int small_device_get(kvs_client *c, const GetTarget &t, uint32_t n, const
   p.tiles_per_combo = fmt.tile_prefix.back();
   p.total_tiles = (uint64_t)n * p.tiles_per_combo;
   p.to_blob = 0;
+  set_copy_facts(&p, t.member_bytes, t.n_members, n);
   cudaEvent_t t0 = nullptr;
   c->time_begin(&t0);
   CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
@@ -2010,6 +2035,7 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
   p.tiles_per_combo = fmt.tile_prefix.back();
   p.total_tiles = (uint64_t)n * p.tiles_per_combo;
   p.to_blob = 0;
+  set_copy_facts(&p, t.member_bytes, t.n_members, n);
   uint64_t payload_per_block = 0;
   for (uint32_t m = 0; m < t.n_members; ++m) payload_per_block += t.member_bytes[m];
   cudaEvent_t t0 = nullptr;
@@ -2189,6 +2215,7 @@ static int get_blocks_impl(kvs_client *c, const GetTarget &t, uint32_t n, const 
       q.blob_ptrs = st2.d<uint64_t>(blobs2);
       q.n_blobs = (uint32_t)nscatter;
       q.total_tiles = (uint64_t)nscatter * q.tiles_per_combo;
+      q.max_member_bytes = q.payload_bytes = 0;  // sources may be pinned host memory: LDG engine
       cudaEvent_t tq = nullptr;
       c->time_begin(&tq);
       CUDA_TRY(launch_copy(q, c->stream, false, c->timeout_flag));

@@ -54,13 +54,17 @@ def _device_index(device: Any) -> int:
     return 0 if d.index is None else d.index
 
 
+_raw_stream = None
+
+
 def _stream_handle(device: int) -> int:
     """The caller's current CUDA stream on `device` as a raw handle."""
-    torch = _torch()
-    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
-    if raw is not None:
-        return raw(device)
-    return torch.cuda.current_stream(device).cuda_stream
+    global _raw_stream
+    if _raw_stream is None:
+        torch = _torch()
+        _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None) or (
+            lambda d: torch.cuda.current_stream(d).cuda_stream)
+    return _raw_stream(device)
 
 
 def _check_tensor(t: Any, device: int, op: str) -> None:
@@ -253,6 +257,7 @@ class PagedLayout:
         self._bytes = (C.c_uint64 * len(members))(*bb)
         self.c = _native.BlockLayout(len(members), members_per_layer, self._ptrs, self._bytes, self.num_blocks)
         self.ref = C.byref(self.c)  # reused by every call
+        self.addr = C.addressof(self.c)  # the same, as an integer for the _fastcall module
 
     @classmethod
     def from_kv_caches(cls, kv_caches: Iterable[Sequence[Any]]) -> "PagedLayout":
@@ -320,6 +325,7 @@ class Client:
         handle = C.c_void_p()
         check(load().kvs_client_create(arr, len(shards), self.device, C.byref(handle)))
         self._h = handle
+        self._hv = handle.value  # the handle as an integer for the _fastcall module; 0 once closed
 
     def _handle(self) -> C.c_void_p:
         if not self._h:
@@ -335,7 +341,7 @@ class Client:
 
     def close(self) -> None:
         if self._h:
-            h, self._h = self._h, None
+            h, self._h, self._hv = self._h, None, 0
             check(load().kvs_client_destroy(h))
 
     def shard_of(self, key: Any) -> int:
@@ -460,6 +466,12 @@ class Client:
     def put_blocks(self, layout: PagedLayout, keys: Any, block_ids: Any, sync_commit: bool = False) -> None:
         if layout.device != self.device:
             raise RuntimeError(f"put_blocks: layout lives on device {layout.device}, client on {self.device}")
+        fast = _native.fastcall
+        if fast is not None and self._hv:  # uint64 / int64 arrays of equal length go straight to the C ABI
+            rc = fast.put_blocks(self._hv, layout.addr, keys, block_ids, sync_commit, _stream_handle(self.device))
+            if rc is not NotImplemented:
+                check(rc)
+                return
         k = _u64_keys(keys)
         b = _i64_array(block_ids)
         if k.shape != b.shape:
@@ -470,6 +482,13 @@ class Client:
     def get_blocks(self, layout: PagedLayout, keys: Any, block_ids: Any) -> np.ndarray:
         if layout.device != self.device:
             raise RuntimeError(f"get_blocks: layout lives on device {layout.device}, client on {self.device}")
+        fast = _native.fastcall
+        if fast is not None and self._hv:  # uint64 / int64 arrays of equal length go straight to the C ABI
+            r = fast.get_blocks(self._hv, layout.addr, keys, block_ids, _stream_handle(self.device))
+            if r.__class__ is np.ndarray:
+                return r
+            if r is not NotImplemented:
+                check(r)
         k = _u64_keys(keys)
         b = _i64_array(block_ids)
         if k.shape != b.shape:
@@ -480,6 +499,13 @@ class Client:
         return found
 
     def exists_batch(self, keys: Any) -> np.ndarray:
+        fast = _native.fastcall
+        if fast is not None and self._hv:
+            r = fast.exists_batch(self._hv, keys)
+            if r.__class__ is np.ndarray:
+                return r
+            if r is not NotImplemented:
+                check(r)
         k = _u64_keys(keys)
         found = np.zeros(k.size, np.bool_)
         check(load().kvs_exists_batch(self._handle(), k.size, _addr(k), _addr(found)))

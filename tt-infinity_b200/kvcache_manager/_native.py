@@ -235,6 +235,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kvs_copy_engine_status": (C.c_int, [C.c_int32, _u32p, _u32p]),
     "kvs_set_copy_wait_limit": (C.c_int, [C.c_int64]),
+    "kvs_set_small_copy_limit": (C.c_int, [C.c_int64]),
 }
 
 _lib = None
@@ -262,7 +263,24 @@ def load(path: str | os.PathLike | None = None):
         )
     if path is None:
         _lib = lib
+        _bind_fastcall(lib)
     return lib
+
+
+fastcall = None  # the CPython module of the block calls' hot path, bound to the loaded library
+
+
+def _bind_fastcall(lib) -> None:
+    """Hands the loaded library's block-call entry points to the _fastcall module (built beside the
+    library by build.py). Without it the facade calls the same entry points through ctypes."""
+    global fastcall
+    try:
+        from . import _fastcall
+    except ImportError:
+        return
+    addr = lambda fn: C.cast(fn, C.c_void_p).value
+    _fastcall.bind(addr(lib.kvs_put_blocks), addr(lib.kvs_get_blocks), addr(lib.kvs_exists_batch))
+    fastcall = _fastcall
 
 
 def check(rc: int) -> None:
