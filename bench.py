@@ -468,7 +468,7 @@ def run_ours(args, rank, local_rank, world):
                             "how": "torch copy of 1 GiB between device memory and pinned host memory, best of 3, "
                                    "CUDA events"},
         "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
-                                     "samples": len(lat),
+                                     "samples": args.latency_samples,
                                      "note": "one committed device-resident block per Client.get_blocks call, "
                                              "timed from the call to its return (the block has landed)",
                                      "engine": "one-wave copy (copies up to 64 MiB)",
@@ -801,7 +801,7 @@ def run_sharded(args, rank, local_rank, world):
                      "while all GPUs copy at once; with shares by rate, by the box's aggregate rate"),
         },
         "get_latency_ms_per_block": {"p50": round(p50, 4), "p99": round(p99, 4), "block_bytes": BLOCK_PAYLOAD,
-                                     "samples": len(lat), "note": "one collective step, every rank gets one block"},
+                                     "samples": args.latency_samples, "note": "one collective step, every rank gets one block"},
         "grant_rounds_per_step": rounds,
         "store": {k2: stats[k2] for k2 in ("writes_through", "victims_evicted", "catalog_replacements", "live_keys")},
         "clocks": clocks,

@@ -517,16 +517,19 @@ struct kvs_client {
     cudaEventCreate(&e);
     return e;
   }
-  void time_begin(cudaEvent_t *start) {
+  void time_begin(cudaEvent_t *start) { time_begin_on(start, stream); }
+  void time_end(cudaEvent_t start, int kind, uint64_t bytes) { time_end_on(start, kind, bytes, stream); }
+  // the same around a launch on stream `on` (the caller's stream, for instance)
+  void time_begin_on(cudaEvent_t *start, cudaStream_t on) {
     *start = nullptr;
     if (!timing) return;
     *start = pooled_event();
-    cudaEventRecord(*start, stream);
+    cudaEventRecord(*start, on);
   }
-  void time_end(cudaEvent_t start, int kind, uint64_t bytes) {
+  void time_end_on(cudaEvent_t start, int kind, uint64_t bytes, cudaStream_t on) {
     if (!timing || !start) return;
     cudaEvent_t stop = pooled_event();
-    cudaEventRecord(stop, stream);
+    cudaEventRecord(stop, on);
     timed.push_back({start, stop, kind, bytes});
   }
   void drain_timing() {
@@ -777,6 +780,30 @@ int block_format(const kvs_block_layout *L, BlockFormat *f) {
     f->tile_prefix[m + 1] = f->tile_prefix[m] + (b + kTileBytes - 1) / kTileBytes;
   }
   f->value_len = off;
+  return KVS_OK;
+}
+
+// block_format through a per-thread cache of the last layout shape (member count, members per
+// layer, member block bytes): the block calls of a serving loop name the same shape every time,
+// so the format is built once per thread instead of once per call. Member pointers are checked
+// for null on every call, as block_format does.
+int cached_block_format(const kvs_block_layout *L, const BlockFormat **out) {
+  thread_local BlockFormat fmt;
+  thread_local std::vector<uint64_t> shape;  // {n_members, members_per_layer, block bytes...}
+  if (L && L->n_members && L->member_ptrs && L->member_block_bytes && shape.size() == 2ull + L->n_members &&
+      shape[0] == L->n_members && shape[1] == L->members_per_layer &&
+      std::memcmp(shape.data() + 2, L->member_block_bytes, 8ull * L->n_members) == 0) {
+    for (uint32_t m = 0; m < L->n_members; ++m)
+      if (!L->member_ptrs[m]) return set_err(KVS_E_INVAL, "block layout: member %u pointer is null", m);
+    *out = &fmt;
+    return KVS_OK;
+  }
+  shape.clear();
+  TRY(block_format(L, &fmt));
+  shape.push_back(L->n_members);
+  shape.push_back(L->members_per_layer);
+  shape.insert(shape.end(), L->member_block_bytes, L->member_block_bytes + L->n_members);
+  *out = &fmt;
   return KVS_OK;
 }
 
@@ -1725,8 +1752,9 @@ static int check_blocks(const kvs_block_layout *L, uint32_t n, const uint64_t *k
 int kvs_put_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, const uint64_t *keys,
                    const int64_t *block_ids, int sync_commit, void *stream) {
   TRY(check_client(c));
-  BlockFormat fmt;
-  TRY(block_format(layout, &fmt));
+  const BlockFormat *fmtp = nullptr;
+  TRY(cached_block_format(layout, &fmtp));
+  const BlockFormat &fmt = *fmtp;
   TRY(check_blocks(layout, n, keys, block_ids, "put_blocks"));
   for (auto *s : c->shards)
     if (fmt.value_len > s->cfg.max_value_bytes)
@@ -1884,8 +1912,13 @@ static int small_device_get(kvs_client *c, const GetTarget &t, uint32_t n, const
     ++hits;
   }
   if (!hits) return KVS_OK;  // every key missed: nothing to copy, no device work to order
-  TRY(begin_op(c, stream));
-  TRY(chain_wait(c, s));
+  // The copy runs on the caller's stream, so it starts after the caller's earlier work on the
+  // destination blocks, and the call synchronises that stream before it returns. Device work of
+  // other clients on this shard is ordered first through the shard's event chain; the shard stays
+  // locked until the copy has finished, so the chain needs no new position.
+  cudaStream_t cs = (cudaStream_t)stream;
+  if (s->tail && std::find(c->chain_evt.begin(), c->chain_evt.end(), s->tail) == c->chain_evt.end())
+    CUDA_TRY(cudaStreamWaitEvent(cs, s->tail, 0));
   const size_t lay_mb = 8ull * t.n_members, lay_rb = lay_mb + 8ull * t.n_members, lay_tp = lay_rb + 8ull * t.n_members;
   p.member_ptrs = reinterpret_cast<const uint64_t *>(c->layout_dev);
   p.member_bytes = reinterpret_cast<const uint64_t *>(c->layout_dev + lay_mb);
@@ -1903,14 +1936,12 @@ static int small_device_get(kvs_client *c, const GetTarget &t, uint32_t n, const
   p.to_blob = 0;
   set_copy_facts(&p, t.member_bytes, t.n_members, n);
   cudaEvent_t t0 = nullptr;
-  c->time_begin(&t0);
-  CUDA_TRY(launch_copy(p, c->stream, true, c->timeout_flag));
-  c->time_end(t0, 1, hits * payload_per_block);
+  c->time_begin_on(&t0, cs);
+  CUDA_TRY(launch_copy(p, cs, true, c->timeout_flag));
+  c->time_end_on(t0, 1, hits * payload_per_block, cs);
   s->launches++;
-  TRY(chain_record(c, shard));
-  CUDA_TRY(cudaStreamSynchronize(c->stream));
+  CUDA_TRY(cudaStreamSynchronize(cs));
   TRY(check_tma_timeouts(c, "get_blocks"));
-  // no end_op: the client stream is idle after the synchronise
   return KVS_OK;
 }
 
@@ -2432,13 +2463,13 @@ int kvs_get_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, co
                    const int64_t *block_ids, uint8_t *found, void *stream) {
   TRY(check_client(c));
   if (!found) return set_err(KVS_E_INVAL, "get_blocks: found is null");
-  BlockFormat fmt;
-  TRY(block_format(layout, &fmt));
+  const BlockFormat *fmt = nullptr;
+  TRY(cached_block_format(layout, &fmt));
   TRY(check_blocks(layout, n, keys, block_ids, "get_blocks"));
   std::lock_guard<std::mutex> lk(c->mu);
   DeviceGuard g(c->device);
   TRY(validate_layout_ptrs(c, layout, "get_blocks"));
-  GetTarget t{&fmt, layout->n_members, layout->member_block_bytes, 1, layout->member_ptrs, nullptr};
+  GetTarget t{fmt, layout->n_members, layout->member_block_bytes, 1, layout->member_ptrs, nullptr};
   return quarantine_on_error(c, get_blocks_impl(c, t, n, keys, block_ids, found, stream));
 }
 
