@@ -9,6 +9,7 @@
 #include "kvs_oracle.h"
 
 #include <pthread.h>
+#include <unistd.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -849,6 +850,39 @@ static int validate_key(kvo_store *s, const uint8_t *key, uint32_t len, const ch
   return KVO_OK;
 }
 
+/* Zeroes a large arena with up to 16 threads, so its pages are faulted in before any timed use
+ * (one thread faults in about 1 GB/s: a 15 GB store took 15 s). */
+typedef struct {
+  uint8_t *p;
+  size_t n;
+} zero_task;
+
+static void *zero_worker(void *arg) {
+  zero_task *t = (zero_task *)arg;
+  memset(t->p, 0, t->n);
+  return NULL;
+}
+
+static void parallel_zero(uint8_t *p, size_t bytes) {
+  long ncpu = sysconf(_SC_NPROCESSORS_ONLN);
+  int nt = bytes < (256u << 20) ? 1 : (int)(ncpu < 1 ? 1 : ncpu > 16 ? 16 : ncpu);
+  pthread_t th[16];
+  zero_task tk[16];
+  const size_t per = (bytes + nt - 1) / nt;
+  int launched = 0;
+  for (int t = 0; t < nt; ++t) {
+    const size_t lo = (size_t)t * per;
+    if (lo >= bytes) break;
+    tk[t].p = p + lo;
+    tk[t].n = bytes - lo < per ? bytes - lo : per;
+    if (t == nt - 1 || pthread_create(&th[t], NULL, zero_worker, &tk[t]) != 0)
+      zero_worker(&tk[t]); /* the last piece (or one whose thread could not start) on this thread */
+    else
+      ++launched;
+  }
+  for (int t = 0; t < launched; ++t) pthread_join(th[t], NULL);
+}
+
 kvo_store *kvo_store_create(const kvo_config *cfg) {
   if (cfg->max_keys == 0 || cfg->unit_bytes == 0 || cfg->max_key_bytes == 0 ||
       cfg->max_key_bytes > KVO_MAX_KEY_BYTES || cfg->heap_bytes < cfg->unit_bytes) {
@@ -872,7 +906,7 @@ kvo_store *kvo_store_create(const kvo_config *cfg) {
   s->lru_head = s->lru_tail = KVO_NONE;
   s->free_head = KVO_NONE;
   s->heap = (uint8_t *)malloc(cfg->heap_bytes);
-  memset(s->heap, 0, cfg->heap_bytes); /* fault the heap in up front, like a reserved arena */
+  parallel_zero(s->heap, cfg->heap_bytes); /* fault the heap in up front, like a reserved arena */
   uint64_t nu = cfg->heap_bytes / cfg->unit_bytes;
   s->num_units = nu > 0xFFFFFFF0ull ? 0xFFFFFFF0u : (uint32_t)nu;
   s->max_order = kvo_floor_log2(s->num_units);
@@ -893,7 +927,7 @@ kvo_store *kvo_store_create(const kvo_config *cfg) {
   s->pool_units_total = cfg->host_pool_bytes / cfg->unit_bytes;
   if (s->pool_units_total) {
     s->pool = (uint8_t *)malloc(s->pool_units_total * cfg->unit_bytes);
-    memset(s->pool, 0, s->pool_units_total * cfg->unit_bytes);
+    parallel_zero(s->pool, s->pool_units_total * cfg->unit_bytes);
     s->pool_free = (free_extent *)malloc(sizeof(free_extent));
     s->pool_free->unit = 0;
     s->pool_free->units = s->pool_units_total;
