@@ -543,18 +543,20 @@ int copy_ctas_per_sm() {
 
 // ---------------------------------------------------------------- token-granular paged fill
 //
-// One CTA per (32-token chunk, group of heads, layer); heads are grouped only as far as needed
-// for about two CTAs per SM. A launch over many layers streams at HBM rate; one layer alone
-// (67 MB for an 8192-token Qwen3 layer) is bound by the kernel's ramp and tail. Every warp
-// resolves the chunk's 32 destinations itself, lane i for token i (last cu_seqlens entry <= token, unsigned so the -1 padding never
+// One CTA per (32-token chunk, group of heads, layer). A launch over many layers uses 256-thread
+// CTAs with heads grouped only as far as needed for about two CTAs per SM, and streams at HBM
+// rate. One layer alone (67 MB for an 8192-token Qwen3 layer) is bound by the kernel's ramp and
+// tail; its launch uses 128-thread CTAs that each move about 2048 words, 16 per thread in two
+// rounds of 8 in flight (measured faster than 4 words in flight per thread, and than one round
+// of 12 or 16, whose registers cut occupancy). Every warp resolves the chunk's 32 destinations
+// itself, lane i for token i (last cu_seqlens entry <= token, unsigned so the -1 padding never
 // matches; then page_table[request][pos / block_size]), and hands them around with shuffles, so
 // no block barrier separates the lookups from the copy (issuing the first round of source loads
-// ahead of the lookups measured 11 % slower on B200). The
-// chunk's source rows are contiguous in the packed input; rows move as 16-byte streaming loads
-// and stores over one flattened (head, K|V, token, word) index. Skips: tokens at or past the
-// valid total (the last cu entry before the -1 padding), page-table entries <= 0 (vLLM's null
-// block, unused slots), and positions or blocks out of range (counted in p.out_of_range instead
-// of being written out of bounds).
+// ahead of the lookups measured 11 % slower on B200). The chunk's source rows are contiguous in
+// the packed input; rows move as 16-byte streaming loads and stores over one flattened (head,
+// K|V, token, word) index. Skips: tokens at or past the valid total (the last cu entry before the
+// -1 padding), page-table entries <= 0 (vLLM's null block, unused slots), and positions or blocks
+// out of range (counted in p.out_of_range instead of being written out of bounds).
 
 constexpr int kFillTokens = 32;
 constexpr int kFillThreads = 256;
@@ -637,7 +639,21 @@ __device__ __forceinline__ long long fill_row_small(const PagedFillParams &p, ui
   return (long long)phys * p.n_heads * p.block_size + pos % p.block_size;
 }
 
-constexpr int kFillUnroll = 4;  // 16-byte words in flight per thread per round
+// Layer pointers of a launch over one layer (the per-layer call): 32 bytes of parameters instead
+// of the 2 KiB FillLayers table.
+struct OneLayer {
+  const uint8_t *k_fill, *v_fill;
+  uint8_t *cache_k, *cache_v;
+};
+
+__device__ __forceinline__ PagedFillParams fill_layer(const PagedFillParams &p0, const OneLayer &L) {
+  PagedFillParams p = p0;
+  p.k_fill = L.k_fill;
+  p.v_fill = L.v_fill;
+  p.cache_k = L.cache_k;
+  p.cache_v = L.cache_v;
+  return p;
+}
 
 __device__ __forceinline__ PagedFillParams fill_layer(const PagedFillParams &p0, const FillLayers &L) {
   PagedFillParams p = p0;  // layer blockIdx.z of the launch
@@ -650,15 +666,20 @@ __device__ __forceinline__ PagedFillParams fill_layer(const PagedFillParams &p0,
 
 // kReq: request r's rows come from its own value (p.req_src, one head of row_bytes per token)
 // instead of the packed fill tensors; see PagedFillParams.
-template <bool kReq>
-__global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFillParams p0, const FillLayers L) {
+// kThreads x kUnroll: threads per CTA and 16-byte words in flight per thread per round.
+// kSmall: fewer than 32 requests (p.batch < 32), whose cu_seqlens and start positions fit the
+// lanes of one warp; kVec: the launcher found every pointer and the row size 16-byte aligned, so
+// the instance holds only the 16-byte path. The launcher picks the instance, so each holds only
+// the code its launch runs.
+template <bool kReq, int kThreads, int kUnroll, class Layers, bool kSmall, bool kVec>
+__global__ void __launch_bounds__(kThreads) paged_fill_kernel(const PagedFillParams p0, const Layers L) {
   const PagedFillParams p = fill_layer(p0, L);
   const uint32_t t0 = blockIdx.x * kFillTokens;
   const uint32_t heads_per = (p.n_heads + gridDim.y - 1) / gridDim.y;
   const uint32_t h0 = blockIdx.y * heads_per;
   const uint32_t h1 = min(p.n_heads, h0 + heads_per);
   const uint32_t lane = threadIdx.x & 31;
-  const bool small = p.batch < 32;
+  constexpr bool small = kSmall;
   uint32_t cu_l = 0xFFFFFFFFu, sp_l = 0;
   uint32_t limit;
   if (small) {
@@ -673,23 +694,13 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
   if (h0 >= h1 || t0 >= limit) return;  // uniform across the CTA
   const uint32_t nt = min((uint32_t)kFillTokens, limit - t0);
   const uint64_t rb = p.row_bytes;
-  const bool vec = ((reinterpret_cast<uint64_t>(p.k_fill) | reinterpret_cast<uint64_t>(p.v_fill) |
-                     reinterpret_cast<uint64_t>(p.cache_k) | reinterpret_cast<uint64_t>(p.cache_v) | rb) & 15u) == 0;
+  const bool vec = kVec || ((reinterpret_cast<uint64_t>(p.k_fill) | reinterpret_cast<uint64_t>(p.v_fill) |
+                             reinterpret_cast<uint64_t>(p.cache_k) | reinterpret_cast<uint64_t>(p.cache_v) | rb) &
+                            15u) == 0;
   if (vec) {
     const uint32_t wpr = (uint32_t)(rb >> 4);  // 16-byte words per row
     const uint32_t per_side = nt * wpr;
     const uint32_t total = (h1 - h0) * 2 * per_side;
-    // word i of the flattened (head, K|V, token, word) index: its source, its token
-    auto src_of = [&](uint32_t i, uint32_t *tok, uint32_t *h, uint32_t *side, uint32_t *in_side) {
-      const uint32_t hs = i / per_side;
-      *in_side = i - hs * per_side;
-      *tok = *in_side / wpr;
-      *h = h0 + (hs >> 1);
-      *side = hs & 1;
-      const uint8_t *src = (*side ? p.v_fill : p.k_fill) + ((uint64_t)*h * p.total_tokens + t0) * rb;
-      return reinterpret_cast<const int4 *>(src) + *in_side;
-    };
-    int4 v[kFillUnroll];
     bool oor = false;
     uint32_t my_req = 0, my_local = 0;
     const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor, &my_req, &my_local)
@@ -702,23 +713,29 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
       my_src = __ldg(p.req_src + my_req) + 2ull * (p.layer0 + blockIdx.z) * my_alloc + (uint64_t)my_local * rb;
     }
     // warp-uniform trip count (every lane joins the shuffles): run while the warp's lane 0 is in range
-    for (uint32_t base = threadIdx.x; base - lane < total; base += kFillThreads * kFillUnroll) {
-      uint64_t dst[kFillUnroll];
+    for (uint32_t base = threadIdx.x; base - lane < total; base += kThreads * kUnroll) {
+      int4 v[kUnroll];
+      uint64_t dst[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kFillUnroll; ++u) {
-        const uint32_t i = base + u * kFillThreads;
+      for (int u = 0; u < kUnroll; ++u) {
+        // word i of the flattened (head, K|V, token, word) index
+        const uint32_t i = base + u * kThreads;
         const bool live = i < total;
-        uint32_t tok = 0, h = 0, side = 0, in_side = 0;
-        const int4 *src = live ? src_of(i, &tok, &h, &side, &in_side) : nullptr;
+        const uint32_t hs = live ? i / per_side : 0;
+        const uint32_t in_side = live ? i - hs * per_side : 0;
+        const uint32_t tok = in_side / wpr;
+        const uint32_t h = h0 + (hs >> 1), side = hs & 1;
         const long long row = __shfl_sync(0xFFFFFFFFu, my_row, tok);
         if (kReq) {
           // the token's row in its value: only tokens that are written have one
           const uint64_t sk = __shfl_sync(0xFFFFFFFFu, my_src, tok);
           const uint64_t sa = __shfl_sync(0xFFFFFFFFu, my_alloc, tok);
-          src = reinterpret_cast<const int4 *>(sk + (side ? sa : 0) + (uint64_t)(in_side - tok * wpr) * 16u);
+          const int4 *src = reinterpret_cast<const int4 *>(sk + (side ? sa : 0) + (uint64_t)(in_side - tok * wpr) * 16u);
           if (live && row >= 0) v[u] = ld_stream(src);
         } else if (live) {
-          v[u] = ld_stream(src);  // in bounds whether or not the token is written
+          // in bounds whether or not the token is written
+          const uint8_t *src = (side ? p.v_fill : p.k_fill) + ((uint64_t)h * p.total_tokens + t0) * rb;
+          v[u] = ld_stream(reinterpret_cast<const int4 *>(src) + in_side);
         }
         dst[u] = 0;
         if (live && row >= 0) {
@@ -728,10 +745,10 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
         }
       }
 #pragma unroll
-      for (int u = 0; u < kFillUnroll; ++u)
+      for (int u = 0; u < kUnroll; ++u)
         if (dst[u]) st_stream(reinterpret_cast<int4 *>(dst[u]), v[u]);
     }
-  } else if (!kReq) {
+  } else if (!kReq && !kVec) {
     bool oor = false;
     uint32_t my_req = 0, my_local = 0;
     const long long my_row = small ? fill_row_small(p, cu_l, sp_l, t0 + lane, lane < nt, &oor, &my_req, &my_local)
@@ -739,7 +756,7 @@ __global__ void __launch_bounds__(kFillThreads) paged_fill_kernel(const PagedFil
     if (oor && threadIdx.x < 32 && blockIdx.y == 0 && blockIdx.z == 0 && p.out_of_range) atomicAdd(p.out_of_range, 1u);
     const uint64_t per_side = (uint64_t)nt * rb;
     const uint64_t total = (uint64_t)(h1 - h0) * 2 * per_side;
-    for (uint64_t base = threadIdx.x; base - lane < total; base += kFillThreads) {
+    for (uint64_t base = threadIdx.x; base - lane < total; base += kThreads) {
       const uint64_t i = base;
       const bool live = i < total;
       const uint64_t hs = live ? i / per_side : 0;
@@ -876,10 +893,43 @@ cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &L, uin
   const uint64_t chunks = (p.total_tokens + kFillTokens - 1) / kFillTokens;
   uint64_t groups = (2 * sms + chunks * n_layers - 1) / (chunks * n_layers);
   groups = groups < 1 ? 1 : (groups > p.n_heads ? p.n_heads : groups);
-  if (p.req_src)
-    paged_fill_kernel<true><<<dim3((unsigned)chunks, (unsigned)groups, n_layers), kFillThreads, 0, stream>>>(p, L);
-  else
-    paged_fill_kernel<false><<<dim3((unsigned)chunks, (unsigned)groups, n_layers), kFillThreads, 0, stream>>>(p, L);
+  if (n_layers == 1 && !p.req_src) {
+    // One layer per call (the reference's interface): 128-thread CTAs, each thread moving 16
+    // words in two rounds of 8, with heads grouped so a CTA holds about 2048 words, and one
+    // layer's pointers as parameters. Measured on B200 for a Qwen3 layer of 8192 tokens, 64
+    // per-layer calls back to back: 14.8-14.9 us per layer against 16.5-16.7 us with the
+    // all-layers configuration below.
+    const uint64_t words_per_head = 2ull * kFillTokens * (p.row_bytes / 16 ? p.row_bytes / 16 : 1);
+    uint64_t heads_per = (128ull * 16) / words_per_head;
+    heads_per = heads_per < 1 ? 1 : heads_per;
+    uint64_t g1 = (p.n_heads + heads_per - 1) / heads_per;
+    const uint64_t want = (4 * sms + chunks - 1) / chunks;  // at least about four CTAs per SM
+    g1 = g1 < want ? want : g1;
+    g1 = g1 > p.n_heads ? p.n_heads : g1;
+    const OneLayer one{L.k_fill[0], L.v_fill[0], L.cache_k[0], L.cache_v[0]};
+    const dim3 grid((unsigned)chunks, (unsigned)g1, 1);
+    const bool vec = ((reinterpret_cast<uint64_t>(one.k_fill) | reinterpret_cast<uint64_t>(one.v_fill) |
+                       reinterpret_cast<uint64_t>(one.cache_k) | reinterpret_cast<uint64_t>(one.cache_v) |
+                       p.row_bytes) & 15u) == 0;
+    if (vec && p.batch < 32)
+      paged_fill_kernel<false, 128, 8, OneLayer, true, true><<<grid, 128, 0, stream>>>(p, one);
+    else if (vec)
+      paged_fill_kernel<false, 128, 8, OneLayer, false, true><<<grid, 128, 0, stream>>>(p, one);
+    else if (p.batch < 32)
+      paged_fill_kernel<false, 128, 8, OneLayer, true, false><<<grid, 128, 0, stream>>>(p, one);
+    else
+      paged_fill_kernel<false, 128, 8, OneLayer, false, false><<<grid, 128, 0, stream>>>(p, one);
+  } else {
+    const dim3 grid((unsigned)chunks, (unsigned)groups, n_layers);
+    if (p.req_src && p.batch < 32)  // the launcher's checks above: 16-byte rows and caches
+      paged_fill_kernel<true, kFillThreads, 4, FillLayers, true, false><<<grid, kFillThreads, 0, stream>>>(p, L);
+    else if (p.req_src)
+      paged_fill_kernel<true, kFillThreads, 4, FillLayers, false, false><<<grid, kFillThreads, 0, stream>>>(p, L);
+    else if (p.batch < 32)
+      paged_fill_kernel<false, kFillThreads, 4, FillLayers, true, false><<<grid, kFillThreads, 0, stream>>>(p, L);
+    else
+      paged_fill_kernel<false, kFillThreads, 4, FillLayers, false, false><<<grid, kFillThreads, 0, stream>>>(p, L);
+  }
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }
