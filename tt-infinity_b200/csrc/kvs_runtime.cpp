@@ -2604,6 +2604,7 @@ int copy_values_launch(kvs_client *c, uint64_t rows, uint64_t value_len, uint32_
   p.tiles_per_combo = meta[4];
   p.total_tiles = (uint64_t)n * p.tiles_per_combo;
   p.to_blob = to_rows ? 0 : 1;
+  set_copy_facts(&p, &value_len, 1, n);
   // rows are this GPU's memory (checked by the caller): the bulk engine when every value address
   // lies in a known slab or peer mapping
   CUDA_TRY(launch_copy(p, c->stream, dev_ranges_hold(addrs, n, value_len), c->timeout_flag));
@@ -2870,6 +2871,7 @@ static int copy_blocks_impl(kvs_client *c, const kvs_block_layout *layout, uint3
   p.tiles_per_combo = fmt.tile_prefix.back();
   p.total_tiles = (uint64_t)n * p.tiles_per_combo;
   p.to_blob = to_blob ? 1 : 0;
+  set_copy_facts(&p, layout->member_block_bytes, layout->n_members, n);
   uint64_t payload = 0;
   for (uint32_t m = 0; m < layout->n_members; ++m) payload += layout->member_block_bytes[m];
   cudaEvent_t t0 = nullptr;
