@@ -471,7 +471,7 @@ def run_ours(args, rank, local_rank, world):
                                      "samples": args.latency_samples,
                                      "note": "one committed device-resident block per Client.get_blocks call, "
                                              "timed from the call to its return (the block has landed)",
-                                     "engine": "one-wave copy (copies up to 64 MiB)",
+                                     "engine": "one-wave copy (copies up to 512 MiB)",
                                      "bulk_engine": {"p50": round(p50_bulk, 4), "p99": round(p99_bulk, 4)}},
         "store": {k: stats[k] for k in ("writes_through", "victims_evicted", "catalog_replacements", "live_keys")},
         "clocks": clocks,
@@ -1114,8 +1114,10 @@ def run_sweep(args):
     rng = np.random.default_rng(9)
     rows = []
     checked = 0
+    client.set_kernel_timing(True)
     for batch in [1, 4, 16, 64, 256, 1024, 4096]:
         put_ms, get_ms = [], []
+        client.kernel_timing()  # reset the totals
         reps = max(2, min(20, 2048 // batch))
         for r in range(reps + 1):
             perm = rng.permutation(FP8_POOL_BLOCKS)
@@ -1129,9 +1131,9 @@ def run_sweep(args):
             client.flush()
             torch.cuda.synchronize()
             t2 = time.perf_counter()
-            found = client.get_blocks(layout, keys, dst)
-            torch.cuda.synchronize()
+            found = client.get_blocks(layout, keys, dst)  # returns once the blocks have landed
             t3 = time.perf_counter()
+            torch.cuda.synchronize()
             assert found.all()
             if r == 0:  # untimed: payload and scale bytes of every restored block equal their sources
                 checked += byte_gate(torch, layout.members, src, dst, 0)["bytes"]
@@ -1141,7 +1143,12 @@ def run_sweep(args):
                 put_ms.append((t1 - t0) * 1e3)
                 get_ms.append((t3 - t2) * 1e3)
         p50p, p50g = statistics.median(put_ms), statistics.median(get_ms)
-        rows.append({"blocks": batch, "bytes": batch * payload,
+        kt = client.kernel_timing()  # every repetition, the untimed first one included
+        kg, ks = kt["gather"], kt["scatter"]
+        kernel = {"gather_ms": round(kg["total_ms"] / max(1, reps + 1), 4),
+                  "scatter_ms": round(ks["total_ms"] / max(1, reps + 1), 4),
+                  "scatter_hbm_frac": round(2 * ks["bytes"] / max(1e-9, ks["total_ms"] / 1e3) / GB / measured_peaks()[0], 4)}
+        rows.append({"blocks": batch, "bytes": batch * payload, "kernels_per_call": kernel,
                      "put_landed_ms_p50": round(p50p, 4), "put_landed_GBps": round(batch * payload / p50p / 1e6, 2),
                      "get_ms_p50": round(p50g, 4), "get_ms_p99": round(sorted(get_ms)[-1], 4),
                      "get_GBps": round(batch * payload / p50g / 1e6, 2), "reps": reps})
@@ -1151,8 +1158,9 @@ def run_sweep(args):
             "pool_blocks": FP8_POOL_BLOCKS, "bytes_per_block": payload, "value_bytes": vlen,
             "parity": {"check": "byte compare of every restored block (payload and scales) with its source, first "
                                 "repetition of every batch size", "bytes": checked},
-            "note": "put = landed (gather into the slab, write-through then flushed outside the put time); get = "
-                    "device-tier hit; wall clock around the Python API call",
+            "note": "put = landed (gather into the slab, then the caller's stream synchronised; the write-through is "
+                    "flushed outside the put time); get = device-tier hit, wall clock around the Python API call, "
+                    "which returns once the blocks have landed",
             "rows": rows}
 
 

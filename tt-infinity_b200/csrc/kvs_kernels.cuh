@@ -1,9 +1,11 @@
 // kvs_kernels.cuh -- device-side data structures and kernel launchers of the B200 KV block store.
 //
 // Four kernel families move every byte and answer every device-side lookup:
-//   * chunk_copy: the paged-block gather (put) / scatter (get) engine. It moves whole member
+//   * chunk_copy: the paged-block gather (put) / scatter (get) engines. They move whole member
 //     blocks between paged KV tensors and packed blobs (device slab values or caller blobs),
-//     16-byte vectorised and coalesced, tiles spread over a persistent grid of 148 x k CTAs.
+//     16-byte vectorised and coalesced: a one-wave grid with one CTA per 16 KiB piece for copies
+//     up to 512 MiB, a persistent grid of one CTA per SM streaming 32 KiB tiles through a bulk-copy
+//     ring for larger ones, and 16-byte loads and stores when a side is host memory.
 //     It restates the byte layout of gather_tp_shards_to_chip / scatter_chunk_from_chip
 //     (patch 0003 gather.hpp lines 9372-9453) for one GPU or for peer GPUs over NVLink.
 //   * index_lookup: a warp-cooperative probe of the shard's device replica of the FNV-1a
@@ -152,7 +154,7 @@ cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream)
 // thread's loads issued before its stores, no tile walk. Needs p.max_member_bytes.
 cudaError_t launch_chunk_copy_small(const ChunkCopyParams &p, cudaStream_t stream);
 // Whether a copy goes to the one-wave variant: its facts are given, it moves at most
-// small_copy_limit() bytes, and its grid stays small. small_copy_limit() is 64 MiB unless
+// small_copy_limit() bytes, and its grid stays small. small_copy_limit() is 512 MiB unless
 // KVS_SMALL_COPY_BYTES sets it (0 turns the variant off); set_small_copy_limit overrides both.
 bool small_copy_suits(const ChunkCopyParams &p);
 uint64_t small_copy_limit();
