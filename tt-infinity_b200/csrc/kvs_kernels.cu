@@ -209,8 +209,12 @@ __global__ void __launch_bounds__(kSmallThreads) chunk_copy_small_kernel(const _
 constexpr int kTmaThreads = 128;
 constexpr int kTmaStages = 6;
 constexpr uint32_t kTmaInflightBytes = 64u << 10;
+constexpr uint64_t kTinyTile = 256;  // unaligned tiles up to this size: one helper thread each
 constexpr uint32_t kTmaTile = 32u << 10;
-constexpr size_t kTmaSmem = (size_t)kTmaStages * kTmaTile;
+// After the ring: the launch's layout arrays (tile prefix, member block bytes, region bases and
+// member pointers) when they fit, so the tile walk reads them from shared memory.
+constexpr size_t kLayoutSmem = 32u << 10;
+constexpr size_t kTmaSmem = (size_t)kTmaStages * kTmaTile + kLayoutSmem;
 constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier waits (seconds at most), then give up
 
 std::atomic<uint32_t> g_wait_polls{kSpinLimit};
@@ -323,11 +327,35 @@ struct TileCursor {
 __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const __grid_constant__ ChunkCopyParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kTmaStages];
+  __shared__ ChunkCopyParams staged;  // p with its layout arrays in shared memory
   const uint32_t tid = threadIdx.x;
   // this CTA's contiguous share of the tiles
   const uint64_t per = (p.total_tiles + gridDim.x - 1) / gridDim.x;
   const uint64_t begin = (uint64_t)blockIdx.x * per;
   const uint64_t end = begin + per < p.total_tiles ? begin + per : p.total_tiles;
+  // Layouts whose arrays fit kLayoutSmem (one member set) are walked from shared memory: a layout
+  // with one tile per member (16 KiB fp8 blocks) and per-block scale members reloads them at
+  // every tile.
+  const uint64_t nm = p.n_members, n_ptrs = p.blob_sets ? 0 : (uint64_t)p.n_ranks * nm;
+  const ChunkCopyParams *lp = &p;
+  if (n_ptrs && 8 * (3 * nm + 1 + n_ptrs) <= kLayoutSmem) {
+    uint64_t *tp = reinterpret_cast<uint64_t *>(smem + (size_t)kTmaStages * kTmaTile);
+    uint64_t *mb = tp + nm + 1, *rb = mb + nm, *mp = rb + nm;
+    for (uint64_t i = tid; i <= nm; i += kTmaThreads) tp[i] = p.tile_prefix[i];
+    for (uint64_t i = tid; i < nm; i += kTmaThreads) {
+      mb[i] = p.member_bytes[i];
+      rb[i] = p.region_bases[i];
+    }
+    for (uint64_t i = tid; i < n_ptrs; i += kTmaThreads) mp[i] = p.member_ptrs[i];
+    if (tid == 0) {
+      staged = p;
+      staged.tile_prefix = tp;
+      staged.member_bytes = mb;
+      staged.region_bases = rb;
+      staged.member_ptrs = mp;
+    }
+    lp = &staged;
+  }
   if (tid == 0) {
     for (int s = 0; s < kTmaStages; ++s)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(&full_bar[s])));
@@ -345,14 +373,29 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const __gri
         if (base) reinterpret_cast<uint32_t *>(base)[w] = p.header_words[w];
       }
     }
+    // Tiles of at most kTinyTile bytes (per-block scales: 4 bytes each, one per layer and block)
+    // go to the helper threads in turn, each thread copying its tile alone, so their dependent
+    // load-store chains run side by side; larger unaligned tiles are copied by all helpers together.
     TileCursor cur;
-    cur.init(&p, begin, end);
+    cur.init(lp, begin, end);
+    uint32_t tiny_seen = 0;  // the same count in every helper thread: the walk is uniform
     for (; cur.t < cur.end; cur.advance()) {
       const TileRef r = cur.ref();
       if (r.skip || tma_ok(r)) continue;
       uint8_t *dst = p.to_blob ? r.blob : r.member;
       const uint8_t *src = p.to_blob ? r.member : r.blob;
-      if (((reinterpret_cast<uint64_t>(dst) | reinterpret_cast<uint64_t>(src) | r.len) & 3u) == 0) {
+      const bool words = ((reinterpret_cast<uint64_t>(dst) | reinterpret_cast<uint64_t>(src) | r.len) & 3u) == 0;
+      if (r.len <= kTinyTile) {
+        if (tiny_seen++ % nh != h) continue;
+        if (words) {
+          for (uint64_t i = 0; i < (r.len >> 2); ++i)
+            reinterpret_cast<uint32_t *>(dst)[i] = reinterpret_cast<const uint32_t *>(src)[i];
+        } else {
+          for (uint64_t i = 0; i < r.len; ++i) dst[i] = src[i];
+        }
+        continue;
+      }
+      if (words) {
         for (uint64_t i = h; i < (r.len >> 2); i += nh)
           reinterpret_cast<uint32_t *>(dst)[i] = reinterpret_cast<const uint32_t *>(src)[i];
       } else {
@@ -365,7 +408,7 @@ __global__ void __launch_bounds__(kTmaThreads) chunk_copy_tma_kernel(const __gri
   const uint32_t smem_base = (uint32_t)__cvta_generic_to_shared(smem);
   TileRef ring[kTmaStages];  // tile of each stage, computed once at load time
   TileCursor cur;
-  cur.init(&p, begin, end);
+  cur.init(lp, begin, end);
   auto next_bulk = [&](TileRef *out) -> bool {
     for (; cur.t < cur.end; cur.advance()) {
       const TileRef r = cur.ref();
