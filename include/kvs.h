@@ -390,9 +390,10 @@ int kvs_copy_engine_status(int32_t device, uint32_t *expired_waits, uint32_t *un
 int kvs_set_copy_wait_limit(int64_t polls);
 /* Copies of at most this many bytes per launch take the one-wave copy engine (one CTA per 16 KiB
  * piece of each member block, all loads in flight at once: lower latency for a few blocks) instead
- * of the persistent engines; process-wide, for launches from now on. 0 turns the one-wave engine
- * off; a negative value restores the default (512 MiB, or KVS_SMALL_COPY_BYTES when set). Every
- * engine moves the same bytes: tests run their cases under each. No counterpart in the reference. */
+ * of the persistent engines, and so does any copy whose member blocks are at most 16 KiB each;
+ * process-wide, for launches from now on. 0 turns the one-wave engine off; a negative value
+ * restores the default (512 MiB, or KVS_SMALL_COPY_BYTES when set). Every engine moves the same
+ * bytes: tests run their cases under each. No counterpart in the reference. */
 int kvs_set_small_copy_limit(int64_t bytes);
 
 /* Per-client kernel timing: with timing on, CUDA events bracket every gather (put) and scatter

@@ -153,8 +153,8 @@ cudaError_t launch_chunk_copy_tma(const ChunkCopyParams &p, cudaStream_t stream)
 // One-wave variant for small copies: one CTA per 16 KiB of each (blob block, rank, member), every
 // thread's loads issued before its stores, no tile walk. Needs p.max_member_bytes.
 cudaError_t launch_chunk_copy_small(const ChunkCopyParams &p, cudaStream_t stream);
-// Whether a copy goes to the one-wave variant: its facts are given, it moves at most
-// small_copy_limit() bytes, and its grid stays small. small_copy_limit() is 512 MiB unless
+// Whether a copy goes to the one-wave variant: its facts are given, and either every member
+// block is one 16 KiB piece or it moves at most small_copy_limit() bytes with a small grid. small_copy_limit() is 512 MiB unless
 // KVS_SMALL_COPY_BYTES sets it (0 turns the variant off); set_small_copy_limit overrides both.
 bool small_copy_suits(const ChunkCopyParams &p);
 uint64_t small_copy_limit();
