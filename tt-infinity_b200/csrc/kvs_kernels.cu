@@ -988,9 +988,9 @@ cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &L, uin
   } else {
     const dim3 grid((unsigned)chunks, (unsigned)groups, n_layers);
     if (p.req_src && p.batch < 32)  // the launcher's checks above: 16-byte rows and caches
-      paged_fill_kernel<true, kFillThreads, 4, FillLayers, true, false><<<grid, kFillThreads, 0, stream>>>(p, L);
+      paged_fill_kernel<true, kFillThreads, 8, FillLayers, true, false><<<grid, kFillThreads, 0, stream>>>(p, L);
     else if (p.req_src)
-      paged_fill_kernel<true, kFillThreads, 4, FillLayers, false, false><<<grid, kFillThreads, 0, stream>>>(p, L);
+      paged_fill_kernel<true, kFillThreads, 8, FillLayers, false, false><<<grid, kFillThreads, 0, stream>>>(p, L);
     else if (p.batch < 32)
       paged_fill_kernel<false, kFillThreads, 4, FillLayers, true, false><<<grid, kFillThreads, 0, stream>>>(p, L);
     else
