@@ -130,7 +130,8 @@ __global__ void __launch_bounds__(kCopyThreads) chunk_copy_kernel(const __grid_c
 // between CUDA events against 15.6 us for the bulk engine, same B200). Scatters of 1 to 128
 // Qwen3 blocks measured on B200 (CUDA events, % of the measured HBM copy bandwidth, one-wave vs
 // bulk): 1 block 39 vs 32, 8 blocks 87 vs 79, 32 blocks (512 MiB) 96.4 vs 95.1, 64 blocks
-// 98.9 vs 98.6, 128 blocks (2 GiB) 100.3 vs 101.1; copies up to kSmallDefaultLimit take this engine.
+// 98.9 vs 98.6, 128 blocks (2 GiB) 100.3 vs 101.1. Copies up to kSmallDefaultLimit take this
+// engine, and so do copies of any size whose member blocks are one piece each (small_copy_suits).
 
 constexpr int kSmallThreads = 256;
 constexpr int kSmallWords = 4;  // 16-byte words per thread

@@ -549,9 +549,10 @@ struct kvs_client {
 
 namespace {
 
-// Copy-engine choice: the one-wave engine for copies of at most a few MiB whose layout facts
-// the caller gave (max_member_bytes, payload_bytes), else the TMA bulk engine for device memory
-// (this GPU's or a peer's) and the LDG/STG engine when a side is host memory.
+// Copy-engine choice, for copies whose layout facts the caller gave (max_member_bytes,
+// payload_bytes): the one-wave engine up to kvs::small_copy_limit() bytes, or at any size when
+// every member block is one 16 KiB piece (kvs::small_copy_suits). Otherwise the TMA bulk engine for
+// device memory (this GPU's or a peer's), and the LDG/STG engine when a side is host memory.
 // KVS_COPY_ENGINE=ldg forces the LDG engine for the copies that do not take the one-wave engine.
 bool tma_enabled() { return kvs::bulk_engine_enabled(); }
 
