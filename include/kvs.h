@@ -282,6 +282,22 @@ int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, c
 int kvs_copy_values(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *addrs, int to_rows,
                     void *stream);
 
+/* Client side: the request records of one sharded step, bucketed by owning shard on the GPU.
+ * keys / ids: n keys and block ids, the first n_get gets, the rest puts. A key's owner is
+ * slot_shard[fnv1a32(key) % 4096] (an int32 placement table), or fnv1a32(key) % world when
+ * slot_shard is null; fnv1a32 runs over the key's 8 little-endian bytes, as kvs_client_shard_of's
+ * does. records: world records of 4 + 4 x cap int64 words, record o = {gets, puts, op, 0, cap get
+ * keys, cap get block ids, cap put keys, cap put block ids}, keys of each kind in batch order,
+ * unused words zero (the layout the step's all-to-all sends). back: [world][2][cap] int32, the
+ * batch position (within its kind) of each placed key; counts: [2][world] int32 keys per (kind,
+ * owner); *overflow: 0, or 1 when an owner got more than cap keys of one kind (the first cap are
+ * placed). Every pointer is device memory of `device`; asynchronous on `stream`. world <= 32.
+ * The reference routes each request to its worker group on the host
+ * (include/kvcache_manager/client.hpp:26-32); this is the GPU bucketing pass of the step. */
+int kvs_bucket_requests(int32_t device, const uint64_t *keys, const int64_t *ids, uint32_t n, uint32_t n_get,
+                        const int32_t *slot_shard, uint32_t world, uint32_t cap, int64_t op, int64_t *records,
+                        int32_t *back, int32_t *counts, uint32_t *overflow, void *stream);
+
 /* ---- token-granular paged KV fill ----
  * Replaces ttnn.experimental.moreh_paged_fill_cache_varlen (patch 0002 lines 106-421: reader /
  * writer kernels, validation at lines 441-545). k_fill / v_fill: [n_heads][total_tokens] rows of

@@ -173,3 +173,25 @@ def test_fastcall_module_is_bound_and_takes_only_exact_arrays(lib):
     assert fast.get_blocks(0, 0, [1, 2, 3], ids, 0) is NotImplemented
     assert fast.get_blocks(0, 0, keys[::2], ids[:2], 0) is NotImplemented  # not contiguous
     assert fast.exists_batch(0, keys.reshape(1, 3)) is NotImplemented
+
+
+def test_bucket_requests_argument_checks_before_any_device_work(lib):
+    """kvs_bucket_requests refuses a bad shard count, capacity, get count or a missing array before
+    it touches a device."""
+    buf = C.create_string_buffer(64)
+    p = C.cast(buf, C.c_void_p)
+    cases = [
+        (0, 8, 0, 0, "world 0 outside"),
+        (33, 8, 0, 0, "world 33 outside"),
+        (2, 0, 0, 0, "cap must be positive"),
+        (2, 8, 1, 2, "2 gets of 1 keys"),
+    ]
+    for world, cap, n, n_get, msg in cases:
+        rc = lib.kvs_bucket_requests(0, p, p, n, n_get, None, world, cap, 0, p, p, p, p, None)
+        assert rc == _native.E_INVAL and msg in lib.kvs_last_error().decode(), (world, cap, n, n_get)
+    assert lib.kvs_bucket_requests(0, None, None, 3, 0, None, 2, 8, 0, p, p, p, p, None) == _native.E_INVAL
+    assert "null argument" in lib.kvs_last_error().decode()
+    assert lib.kvs_bucket_requests(0, p, p, 1, 0, None, 2, 8, 0, p, p, p, None, None) == _native.E_INVAL
+    # host memory is refused (device memory of the named GPU only)
+    assert lib.kvs_bucket_requests(0, p, p, 1, 0, None, 2, 8, 0, p, p, p, p, None) == _native.E_INVAL
+    assert "device memory" in lib.kvs_last_error().decode()

@@ -572,6 +572,85 @@ __global__ void apply_mutations_kernel(const MutationParams p) {
   }
 }
 
+// ---------------------------------------------------------------- request bucketing (sharded step)
+//
+// One CTA of kBucketThreads threads: zero the records, then walk the keys in chunks of one key per
+// thread. For each of the 2 x world groups (kind, owner) a ballot per warp gives each key its rank
+// among the chunk's keys of that group (popc of the lower lanes, plus the group's count in earlier
+// warps from a shared-memory scan), so the order within a group is batch order -- the stable order
+// the owner's catalog sees on the host path.
+
+constexpr int kBucketThreads = 1024;
+constexpr int kBucketWarps = kBucketThreads / 32;
+constexpr uint32_t kBucketMaxGroups = 64;  // 2 x world for up to 32 shards
+
+__global__ void __launch_bounds__(kBucketThreads) bucket_requests_kernel(const BucketParams p) {
+  __shared__ uint32_t warp_count[kBucketMaxGroups][kBucketWarps];
+  __shared__ uint32_t group_base[kBucketMaxGroups];
+  const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t groups = 2 * p.world;
+  const uint64_t words = (uint64_t)p.world * request_record_words(p.cap);
+  for (uint64_t i = tid; i < words; i += kBucketThreads) p.records[i] = 0;
+  for (uint32_t g = tid; g < groups; g += kBucketThreads) group_base[g] = 0;
+  if (tid == 0) *p.overflow = 0u;
+  __syncthreads();
+  for (uint32_t base = 0; base < p.n; base += kBucketThreads) {
+    const uint32_t i = base + tid;
+    const bool live = i < p.n;
+    uint32_t group = 0xFFFFFFFFu;
+    uint64_t key = 0;
+    if (live) {
+      key = p.keys[i];
+      uint32_t h = 2166136261u;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        h ^= (uint32_t)((key >> (8 * b)) & 0xFFu);
+        h *= 16777619u;
+      }
+      const uint32_t owner = p.slot_shard ? (uint32_t)p.slot_shard[h % kPlacementSlots] : h % p.world;
+      group = (i < p.n_get ? 0u : p.world) + owner;
+    }
+    uint32_t my_rank = 0;
+    for (uint32_t g = 0; g < groups; ++g) {
+      const uint32_t vote = __ballot_sync(0xFFFFFFFFu, group == g);
+      if (group == g) my_rank = __popc(vote & ((1u << lane) - 1u));
+      if (lane == 0) warp_count[g][warp] = __popc(vote);
+    }
+    __syncthreads();
+    // per group: exclusive scan of the warp counts (one thread per group), then the chunk total
+    if (tid < groups) {
+      uint32_t run = group_base[tid];
+      for (int w = 0; w < kBucketWarps; ++w) {
+        const uint32_t c = warp_count[tid][w];
+        warp_count[tid][w] = run;
+        run += c;
+      }
+      group_base[tid] = run;
+    }
+    __syncthreads();
+    if (live) {
+      const uint32_t rank = warp_count[group][warp] + my_rank;
+      const uint32_t kind = group >= p.world, owner = group - kind * p.world;
+      if (rank < p.cap) {
+        int64_t *rec = p.records + (uint64_t)owner * request_record_words(p.cap) + 4 + 2ull * p.cap * kind;
+        rec[rank] = (int64_t)key;
+        rec[p.cap + rank] = p.ids[i];
+        p.back[((uint64_t)owner * 2 + kind) * p.cap + rank] = (int32_t)(i - kind * p.n_get);
+      } else {
+        *p.overflow = 1u;
+      }
+    }
+    __syncthreads();  // warp_count is rewritten by the next chunk
+  }
+  for (uint32_t g = tid; g < groups; g += kBucketThreads) {
+    const uint32_t kind = g >= p.world, owner = g - kind * p.world;
+    const uint32_t c = group_base[g] < p.cap ? group_base[g] : p.cap;
+    p.records[(uint64_t)owner * request_record_words(p.cap) + kind] = c;
+    p.counts[kind * p.world + owner] = (int32_t)c;
+    if (kind == 0) p.records[(uint64_t)owner * request_record_words(p.cap) + 2] = p.op;
+  }
+}
+
 __global__ void echo_kernel(const uint8_t *in, uint8_t *out, uint32_t n) {
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
     out[i] = in[i];
@@ -1004,6 +1083,13 @@ cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &L, uin
 cudaError_t launch_echo(const uint8_t *in, uint8_t *out, uint32_t n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   echo_kernel<<<1, 256, 0, stream>>>(in, out, n);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bucket_requests(const BucketParams &p, cudaStream_t stream) {
+  if (p.world == 0 || 2 * p.world > kBucketMaxGroups || p.cap == 0) return cudaErrorInvalidValue;
+  bucket_requests_kernel<<<1, kBucketThreads, 0, stream>>>(p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }

@@ -174,6 +174,29 @@ cudaError_t launch_paged_fill(const PagedFillParams &p, const FillLayers &layers
                               cudaStream_t stream);
 cudaError_t launch_echo(const uint8_t *in, uint8_t *out, uint32_t n, cudaStream_t stream);
 
+// Request records of one hash-sharded step, bucketed on the GPU. Keys 0 .. n_get - 1 are gets,
+// n_get .. n - 1 puts. Each key's owner is slot_shard[fnv1a32(key) % kPlacementSlots] (or
+// fnv1a32(key) % world without a table). Record o (request_record_words(cap) int64 words) holds
+// {gets, puts, op, 0}, then cap get keys, cap get block ids, cap put keys, cap put block ids, in
+// batch order within each kind; unused words are zero. back[(o * 2 + kind) * cap + j] is the batch
+// position (within its kind) of the j-th key of that kind in record o, counts[kind * world + o] the
+// number of keys. *overflow is 0 after the launch, or 1 if a group had more than cap keys (it keeps
+// its first cap keys).
+constexpr uint32_t kPlacementSlots = 4096;
+__host__ __device__ inline uint64_t request_record_words(uint32_t cap) { return 4 + 4ull * cap; }
+struct BucketParams {
+  const uint64_t *keys;
+  const int64_t *ids;
+  uint32_t n, n_get, world, cap;
+  const int32_t *slot_shard;  // [kPlacementSlots] or nullptr
+  int64_t op;
+  int64_t *records;           // [world][request_record_words(cap)]
+  int32_t *back;              // [world][2][cap]
+  int32_t *counts;            // [2][world]
+  uint32_t *overflow;         // one word
+};
+cudaError_t launch_bucket_requests(const BucketParams &p, cudaStream_t stream);
+
 // Host-side FNV-1a 32 (the same function the device probe computes).
 inline uint32_t fnv1a32(const uint8_t *key, uint32_t len) {
   uint32_t h = 2166136261u;

@@ -2890,6 +2890,29 @@ int kvs_copy_blocks(kvs_client *c, const kvs_block_layout *layout, uint32_t n, c
   return quarantine_on_error(c, copy_blocks_impl(c, layout, n, block_ids, blob_addrs, to_blob, stream));
 }
 
+int kvs_bucket_requests(int32_t device, const uint64_t *keys, const int64_t *ids, uint32_t n, uint32_t n_get,
+                        const int32_t *slot_shard, uint32_t world, uint32_t cap, int64_t op, int64_t *records,
+                        int32_t *back, int32_t *counts, uint32_t *overflow, void *stream) {
+  if (world == 0 || world > 32) return set_err(KVS_E_INVAL, "bucket_requests: world %u outside 1..32", world);
+  if (cap == 0) return set_err(KVS_E_INVAL, "bucket_requests: cap must be positive");
+  if (n_get > n) return set_err(KVS_E_INVAL, "bucket_requests: %u gets of %u keys", n_get, n);
+  if ((n && (!keys || !ids)) || !records || !back || !counts || !overflow)
+    return set_err(KVS_E_INVAL, "bucket_requests: null argument");
+  const void *ptrs[] = {keys, ids, slot_shard, records, back, counts, overflow};
+  for (const void *q : ptrs) {
+    if (!q) continue;
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, q) != cudaSuccess || a.type != cudaMemoryTypeDevice || a.device != device) {
+      cudaGetLastError();
+      return set_err(KVS_E_INVAL, "bucket_requests: every array must be device memory of device %d", device);
+    }
+  }
+  DeviceGuard g(device);
+  kvs::BucketParams p{keys, ids, n, n_get, world, cap, slot_shard, op, records, back, counts, overflow};
+  CUDA_TRY(kvs::launch_bucket_requests(p, (cudaStream_t)stream));
+  return KVS_OK;
+}
+
 int kvs_copy_values(kvs_client *c, void *rows, uint64_t value_len, uint32_t n, const uint64_t *addrs, int to_rows,
                     void *stream) {
   TRY(check_client(c));

@@ -236,6 +236,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kvs_copy_engine_status": (C.c_int, [C.c_int32, _u32p, _u32p]),
     "kvs_set_copy_wait_limit": (C.c_int, [C.c_int64]),
     "kvs_set_small_copy_limit": (C.c_int, [C.c_int64]),
+    "kvs_bucket_requests": (C.c_int, [C.c_int32, P, P, C.c_uint32, C.c_uint32, P, C.c_uint32, C.c_uint32, C.c_int64,
+                                      P, P, P, P, P]),
 }
 
 _lib = None

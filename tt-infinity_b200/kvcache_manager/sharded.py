@@ -301,6 +301,67 @@ class DeviceEngine:
         return self.server.stats()
 
 
+class _GpuBucketing:
+    """The step's request records built on the GPU (kvs_bucket_requests) of a store on NCCL ranks:
+    keys and block ids go up in one pinned copy each, one kernel buckets them by owner into the
+    all-to-all's send records, and the received records come back to the host in one copy together
+    with this rank's batch positions per owner."""
+
+    def __init__(self, store: "ShardedStore") -> None:
+        torch = store._torch
+        w, cap, dev = store.world, store.cap, store._dev
+        self.store = store
+        self.n_max = 2 * w * cap
+        self.h_keys = torch.empty(self.n_max, dtype=torch.int64).pin_memory()
+        self.h_ids = torch.empty(self.n_max, dtype=torch.int64).pin_memory()
+        self.d_keys = torch.empty(self.n_max, dtype=torch.int64, device=dev)
+        self.d_ids = torch.empty(self.n_max, dtype=torch.int64, device=dev)
+        self.rec_words = request_words(cap)
+        self.send = torch.empty(w * self.rec_words, dtype=torch.int64, device=dev)
+        # one buffer comes back: received records, then back [w][2][cap] int32, counts [2][w] int32
+        # and the overflow word (int32 views of its int64 tail)
+        self.r_words = w * self.rec_words
+        tail = (2 * w * cap + 2 * w + 2 + 1) // 2
+        self.out = torch.zeros(self.r_words + tail, dtype=torch.int64, device=dev)
+        t32 = self.out[self.r_words:].view(torch.int32)
+        self.back = t32[:2 * w * cap]
+        self.counts = t32[2 * w * cap:2 * w * cap + 2 * w]
+        self.overflow = t32[2 * w * cap + 2 * w:2 * w * cap + 2 * w + 1]
+        self.table = None
+        if store.table is not None:
+            self.table = torch.from_numpy(np.ascontiguousarray(store.table, dtype=np.int32)).to(dev)
+
+    def exchange(self, op: int, gk: np.ndarray, gi: np.ndarray, pk: np.ndarray, pi: np.ndarray):
+        st = self.store
+        torch, w, cap = st._torch, st.world, st.cap
+        ng, n = gk.size, gk.size + pk.size
+        if n > self.n_max:
+            raise ValueError(f"sharded store: more than {cap} keys for one shard in a step")
+        hk, hi = self.h_keys.numpy(), self.h_ids.numpy()
+        hk[:ng], hk[ng:n] = gk.view(np.int64), pk.view(np.int64)
+        hi[:ng], hi[ng:n] = gi, pi
+        if n:
+            self.d_keys[:n].copy_(self.h_keys[:n], non_blocking=True)
+            self.d_ids[:n].copy_(self.h_ids[:n], non_blocking=True)
+        stream = torch.cuda.current_stream(st._dev).cuda_stream
+        ptr = lambda t: C.c_void_p(t.data_ptr())
+        check(load().kvs_bucket_requests(
+            st.engine.device, ptr(self.d_keys), ptr(self.d_ids), n, ng,
+            ptr(self.table) if self.table is not None else None, w, cap, op, ptr(self.send), ptr(self.back),
+            ptr(self.counts), ptr(self.overflow), C.c_void_p(stream)))
+        st.dist.all_to_all_single(self.out[:self.r_words], self.send, group=st.group)
+        host = self.out.cpu().numpy()
+        t32 = host[self.r_words:].view(np.int32)
+        back = t32[:2 * w * cap].reshape(w, 2, cap)
+        counts = t32[2 * w * cap:2 * w * cap + 2 * w].reshape(2, w)
+        if t32[2 * w * cap + 2 * w]:
+            raise ValueError(f"sharded store: more than {cap} keys for one shard in a step")
+        reqs = unpack_requests(host[:self.r_words].reshape(w, self.rec_words), cap)
+        g_pos = [back[o, 0, :counts[0, o]].astype(np.int64) for o in range(w)]
+        p_pos = [back[o, 1, :counts[1, o]].astype(np.int64) for o in range(w)]
+        return reqs, g_pos, p_pos
+
+
 class ShardedStore:
     """Collective put / get / exists of paged KV blocks over a store sharded one shard per rank.
 
@@ -346,6 +407,7 @@ class ShardedStore:
         self._token = torch.zeros(1, dtype=torch.int32, device=self._dev)
         self._rows_out = None
         self._rows_in = None
+        self._bucket = _GpuBucketing(self) if self._cuda else None
         self.steps = 0
         # blocks moved by this rank: as a client (puts sent, gets found) and as an owner (gets
         # served); "remote" ones crossed to or from another GPU
@@ -354,6 +416,16 @@ class ShardedStore:
         self.closed = False
 
     # ---- collectives
+    def _requests(self, op: int, gk: np.ndarray, gi: np.ndarray, pk: np.ndarray, pi: np.ndarray):
+        """Request records exchanged with every rank: per source rank (get keys, get ids, put keys,
+        put ids), and per owner the batch positions of this rank's gets and puts. On GPUs the keys
+        are bucketed on the device and the records go to the all-to-all from device memory; on CPU
+        ranks pack_requests buckets them with numpy."""
+        if self._bucket is not None:
+            return self._bucket.exchange(op, gk, gi, pk, pi)
+        send, g_pos, p_pos = pack_requests(self.world, self.cap, op, gk, gi, pk, pi, self.table)
+        return unpack_requests(self._alltoall(send), self.cap), g_pos, p_pos
+
     def _alltoall(self, send: np.ndarray) -> np.ndarray:
         torch = self._torch
         s = torch.from_numpy(np.ascontiguousarray(send)).reshape(-1)
@@ -416,8 +488,7 @@ class ShardedStore:
         if self.closed:
             raise KvsError(_native.E_CLOSED, "sharded store is closed")
         world, cap, eng = self.world, self.cap, self.engine
-        send, g_pos, p_pos = pack_requests(world, cap, 0, gk, gi, pk, pi, self.table)
-        reqs = unpack_requests(self._alltoall(send), cap)
+        reqs, g_pos, p_pos = self._requests(0, gk, gi, pk, pi)
         # ---- owner: gets of every source, in source-rank order
         n_get = [r[0].size for r in reqs]
         g_keys = np.concatenate([r[0] for r in reqs]) if sum(n_get) else np.zeros(0, np.uint64)
@@ -544,9 +615,8 @@ class ShardedStore:
         """Collective exists of this rank's keys (commit barrier on every owner first)."""
         k = np.ascontiguousarray(np.asarray(keys, dtype=np.uint64).reshape(-1))
         world, cap = self.world, self.cap
-        send, g_pos, _ = pack_requests(world, cap, 1, k, np.zeros(k.size, np.int64), np.zeros(0, np.uint64),
-                                       np.zeros(0, np.int64), self.table)
-        reqs = unpack_requests(self._alltoall(send), cap)
+        reqs, g_pos, _ = self._requests(1, k, np.zeros(k.size, np.int64), np.zeros(0, np.uint64),
+                                        np.zeros(0, np.int64))
         n = [r[0].size for r in reqs]
         keys_all = np.concatenate([r[0] for r in reqs]) if sum(n) else np.zeros(0, np.uint64)
         found = self.engine.exists(keys_all)
