@@ -88,6 +88,9 @@ def parse() -> argparse.Namespace:
                     help="the connector's batched restore of a Qwen3-32B-shaped 8192-token prompt (64 layers)")
     ap.add_argument("--fill", action="store_true",
                     help="token-granular paged fill: 8192 tokens of 4 requests into 64 layers' caches")
+    ap.add_argument("--ref-blocks", type=int, default=0,
+                    help="--impl reference: blocks put and got per step (default: the GPU step's 128); the CPU "
+                         "tests use a few to check the line's contract quickly")
     ap.add_argument("--resident", type=int, default=0,
                     help="--mix: resident blocks per GPU (default: 1M / N, capped so that the pinned host "
                          "tier, which mirrors every resident block, stays within 35%% of the host's available memory)")
@@ -1056,7 +1059,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     threads = cpu_threads()
-    n = BATCH_BLOCKS
+    n = args.ref_blocks or BATCH_BLOCKS
     gbps, dt = cpu_run(n, args.steps, threads, warmup=args.warmup)
     return {
         "metric": METRIC, "value": round(gbps, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,

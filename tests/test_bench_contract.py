@@ -19,7 +19,7 @@ def _run(*args, timeout=600):
 
 
 def test_reference_arm_prints_one_contract_line():
-    r = _run("--impl", "reference", "--steps", "1", "--warmup", "1")
+    r = _run("--impl", "reference", "--steps", "1", "--warmup", "1", "--ref-blocks", "8")
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
