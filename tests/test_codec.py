@@ -88,3 +88,23 @@ def test_header_words_padding():
     assert len(codec.header_words(1, [5])) * 4 % 32 == 0
     assert codec.header_words(6, [1] * 6)[:2] == [codec.MAGIC, 6]
     assert codec.header_words(64, [1] * 64)[-1] == 0 and len(codec.header_words(64, [1] * 64)) == 72
+
+
+def test_chunk_span_checks_like_chunk_slots(golden_dir):
+    """The numpy form used by the batched restore raises what _chunk_slots raises and returns the
+    first slot and the count of every accepted case, for lists, numpy arrays and CPU tensors."""
+    import numpy as np
+    import torch
+
+    fx = _load(golden_dir, "raw_byte_plans.json")
+    c = codec.RawByteCodec(tp_size=2, dp_size=1, block_size=32, blocks_per_dp=64, shard_block_bytes=2048)
+    for case in fx["chunk_slots_rejects"]:
+        exc = {"ValueError": ValueError, "RuntimeError": RuntimeError}[case["error"]]
+        for form in (list, np.array, lambda x: torch.tensor(x, dtype=torch.int64)):
+            with pytest.raises(exc) as err:
+                c._chunk_span(form(case["slots"]))
+            assert str(err.value).split("(")[0].split(". The")[0].strip() in case["message"]
+    for case in fx["chunk_slots_accepts"]:
+        slots = c._chunk_slots(case["slots"])
+        for form in (list, np.array, lambda x: torch.tensor(x, dtype=torch.int64)):
+            assert c._chunk_span(form(case["slots"])) == (slots[0], len(slots))

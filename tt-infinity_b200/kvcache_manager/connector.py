@@ -166,14 +166,14 @@ class KVCacheClient:
         if bs != self.raw_codec.block_size:
             raise ValueError(f"cache blocks hold {bs} tokens, not block_size {self.raw_codec.block_size}")
         row_bytes = int(k0[0, 0].numel() * k0.element_size())
-        slots = [self.raw_codec._chunk_slots(sl) for sl in slot_mapping_slices]
-        tokens = np.array([len(x) for x in slots], np.uint32)
+        spans = [self.raw_codec._chunk_span(sl) for sl in slot_mapping_slices]
+        tokens = np.array([cnt for _, cnt in spans], np.uint32)
         max_blocks = int(max(-(-int(t) // bs) for t in tokens))
         # a chunk starts on a block boundary with sequential slots: its blocks follow its first one
         page = np.zeros((n, max_blocks), np.int32)
-        for i, x in enumerate(slots):
-            nb = -(-len(x) // bs)
-            page[i, :nb] = np.arange(x[0] // bs, x[0] // bs + nb, dtype=np.int32)
+        for i, (first, cnt) in enumerate(spans):
+            nb = -(-cnt // bs)
+            page[i, :nb] = np.arange(first // bs, first // bs + nb, dtype=np.int32)
         starts = np.zeros(n, np.int32)
         raw = [self.raw_key(k) for k in keys]
         key_arr = (C.c_void_p * n)(*[C.cast(C.c_char_p(b), C.c_void_p) for b in raw])
