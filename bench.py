@@ -465,6 +465,7 @@ def run_ours(args, rank, local_rank, world):
             "scatter_get": {"launches": s["launches"], "avg_ms": round(s["total_ms"] / max(1, s["launches"]), 4),
                             "GBps_2x_payload": round(2 * s["bytes"] / max(1e-9, s["total_ms"] / 1e3) / GB, 1)},
         },
+        "device_paths": device_path_rates(None, None, None, timing, 1),
         "write_through": write_through_summary(wt, BATCH_BLOCKS * BLOCK_PAYLOAD * args.steps, best),
         "step_split_ms": step_split(elapsed_ms, args.steps, g, s, wt),
         "pcie_peaks_GBps": {"d2h": round(best, 2), "h2d": round(h2d_best, 2),
@@ -532,6 +533,24 @@ def _peer_copy_rates(torch, dist, device, nbytes=1 << 30):
     dist.barrier()
     del buf, src
     return best, -_max_over_ranks(torch, dist, -best, device)
+
+
+def device_path_rates(torch, dist, device, timing, world):
+    """Payload GB/s of the copy kernels alone, over all ranks: the put (gather) and get (scatter)
+    kernels' payload bytes per launch, summed over ranks, over the slowest rank's average launch
+    time. The step's value also waits for the host write-through; these show what the device
+    paths move (at N > 1 they include the P2P stores over NVLink)."""
+    out = {}
+    for name, t in (("put", timing["gather"]), ("get", timing["scatter"])):
+        launches = max(1, t["launches"])
+        per_launch, ms = t["bytes"] / launches, t["total_ms"] / launches
+        if world > 1:
+            per_launch = _sum_over_ranks(torch, dist, per_launch, device)
+            ms = _max_over_ranks(torch, dist, ms, device)
+        out[name + "_GBps"] = round(per_launch / max(ms / 1e3, 1e-12) / GB, 1)
+    out["how"] = ("payload bytes per launch summed over ranks / the slowest rank's average launch time (CUDA "
+                  "events); the step's value also waits for the write-through")
+    return out
 
 
 def _max_over_ranks(torch, dist, value, device):
@@ -706,6 +725,7 @@ def run_sharded(args, rank, local_rank, world):
     wt_gbps_min = -_max_over_ranks(torch, dist, -wt_gbps, device)
     value = world * args.steps * step_bytes / (elapsed_ms / 1e3) / GB
     dom, kernels, nvlink_achieved = _nvlink_roofline(torch, dist, device, timing, c0, c1, BLOCK_PAYLOAD)
+    paths = device_path_rates(torch, dist, device, timing, world)
 
     # e2e: the public sharded API with host key / block-table arrays, wall clock (max over ranks)
     torch.cuda.synchronize()
@@ -782,6 +802,7 @@ def run_sharded(args, rank, local_rank, world):
             "hbm_peak": hbm_peak, "hbm_peak_kind": peak_kind,
         },
         "kernels": kernels,
+        "device_paths": paths,
         "limiter": {
             "step_ms": round(elapsed_ms / args.steps, 3),
             "write_through_ms_slowest_shard": round(wt_ms_max, 3),
