@@ -110,6 +110,7 @@ static PyObject *put_blocks(PyObject *self, PyObject *const *args, Py_ssize_t na
   void *client = PyLong_AsVoidPtr(args[0]);
   const void *layout = PyLong_AsVoidPtr(args[1]);
   const int sync_commit = PyObject_IsTrue(args[4]);
+  if (sync_commit < 0) return NULL;
   void *stream = PyLong_AsVoidPtr(args[5]);
   if (PyErr_Occurred()) return NULL;
   Py_buffer k, b;
