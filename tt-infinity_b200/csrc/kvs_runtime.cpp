@@ -8,7 +8,12 @@
 //     packs its metadata into the staging area, uploads it with one copy, and launches its
 //     kernels on the client stream. Work that touches a shard is ordered across clients by an
 //     event chain kept under the shard mutex: each call waits on the shard's last event before
-//     launching and records a new one after.
+//     launching and records a new one after. A get of at most kvs::kInlineKeys device-resident
+//     blocks is the exception: the catalog answers its lookups and its one copy runs on the
+//     caller's stream, which the call synchronises before returning (small_device_get).
+//   * Copies take one of three engines (launch_copy): the one-wave engine for copies up to
+//     kvs::small_copy_limit() bytes or of one-piece member blocks, the bulk-copy ring for larger
+//     device-memory copies, and 16-byte loads and stores when a side is host memory.
 //   * Host write-through is a device->host copy of each landed value on the shard's
 //     write-through stream, ordered after the gather by an event; the pending-host FIFO entry
 //     becomes committed at the next commit barrier (or earlier when allocation pressure forces
